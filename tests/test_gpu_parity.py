@@ -1,0 +1,362 @@
+"""Parity of the CUDA path (through the C-ABI) with the CPU oracle and with the
+reference's own golden vectors.  Bit-exact for integer / index / grouped-fold
+work and for every family whose reference arithmetic the kernel restates;
+the bf16 contraction is held to the BASELINE tolerance (1e-2 relative)."""
+import hashlib
+
+import numpy as np
+import pytest
+
+from golden_util import bits_of, f, fbits, fvals, h, load, prng_values, seeded_normal, seeded_uniform
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+G = load()
+
+
+@pytest.fixture(scope="module")
+def fam():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from tiler_b200 import families
+    families.context()
+    return families
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def assert_bits_equal(got, want, what=""):
+    g = np.ascontiguousarray(got).view(np.uint32).ravel()
+    w = np.ascontiguousarray(want).view(np.uint32).ravel()
+    bad = np.nonzero(g != w)[0]
+    assert bad.size == 0, f"{what}: {bad.size} mismatches, first at {bad[:5]}: got {g[bad[:5]]} want {w[bad[:5]]}"
+
+
+# ---- golden vectors through the CUDA path -----------------------------------
+
+def test_silu_boundary_corpus_on_device(fam):
+    args = fbits([a for a, _ in G["silu"]["cases"]])
+    y = host(fam.silu(cuda(args)))
+    assert bits_of(y) == [h(w) for _, w in G["silu"]["cases"]]
+
+
+def test_rms_norm_corpus_on_device(fam):
+    eps = h(G["rms_norm"]["eps_bits"])
+    for case in G["rms_norm"]["cases"]:
+        x = (fbits(case["x_bits"]) if "x_bits" in case else fvals(case["x"]))[None, :]
+        w = np.array(case["w"], np.float32)
+        y = host(fam.rms_norm(cuda(x), cuda(w), eps))
+        assert bits_of(y) == [h(v) for v in case["y"]], case["cite"]
+    for case in G["rms_norm"]["uniform"]:
+        x = np.full((1, case["extent"]), case["fill"], np.float32)
+        if case["hole_last"]:
+            x[0, -1] = 0
+        y = bits_of(host(fam.rms_norm(cuda(x), cuda(np.ones(case["extent"], np.float32)), eps)))
+        assert y[0] == h(case["y0"]) and y[-1] == h(case["ylast"]), case["cite"]
+
+
+def test_softmax_corpus_on_device(fam):
+    for case in G["softmax"]["cases"]:
+        x = (fbits(case["x_bits"]) if "x_bits" in case else fvals(case["x"]))[None, :]
+        y = host(fam.softmax(cuda(x)))
+        want = [h(case["y_all"])] * x.size if "y_all" in case else [h(v) for v in case["y"]]
+        assert bits_of(y) == want, case["cite"]
+
+
+def test_sum_goldens_on_device(fam):
+    S = G["sums"]
+    for case in S["strict"]:
+        x = (fbits(case["x_bits"]) if "x_bits" in case else fvals(case["x"])).reshape(case["rows"], case["count"])
+        y = host(fam.strict_sum_f32(cuda(x)))
+        want = [h(v) for v in case["y"]] if isinstance(case["y"][0], str) else bits_of(case["y"])
+        assert bits_of(y) == want
+    for case in S["partitioned"]:
+        x = (fbits(case["x_bits"]) if "x_bits" in case else fvals(case["x"])).reshape(case["rows"], case["count"])
+        y = host(fam.partitioned_sum_f32(cuda(x), case["partitions"], case["per"]))
+        want = [h(v) for v in case["y_bits"]] if "y_bits" in case else bits_of(case["y"])
+        assert bits_of(y) == want, case["cite"]
+    for case in S["cooperative"]:
+        x = fvals(case["x"]).reshape(case["rows"], case["count"])
+        y = host(fam.cooperative_sum_f32(cuda(x), case["participants"], case["per"], case["rounds"],
+                                         case["participant_major"]))
+        if "y" in case:
+            assert bits_of(y) == bits_of(case["y"])
+        else:
+            assert bits_of(y)[0] == bits_of([case["y0"]])[0]
+
+
+def test_quantize_affine_goldens_on_device(fam):
+    for c in G["quantize_affine"]["quantize"]:
+        x = fbits([c["x_bits"]]) if "x_bits" in c else np.array([c["x"]], np.float32)
+        codes = host(fam.quantize_affine_u8(cuda(x), c["scale"], c["zero_point"], c["maximum"]))
+        assert int(codes[0]) == c["code"]
+    for nb in G["quantize_affine"]["nan_refused"]:
+        with pytest.raises(fam.TilerCudaError) as e:
+            fam.quantize_affine_u8(cuda(fbits(["0x3f800000", nb])), 0.5, 8, 15)
+        assert e.value.code == 4 and e.value.position == 1
+    for c in G["quantize_affine"]["dequantize"]:
+        y = host(fam.dequantize_affine_u8(cuda(np.array([c["code"]], np.uint8)), c["scale"], c["zero_point"]))
+        assert bits_of(y)[0] == h(c["y_bits"])
+
+
+def test_gather_conformance_on_device(fam):
+    Gt = G["gather"]
+    table = np.arange(15, dtype=np.int32).reshape(5, 3)
+    for case in Gt["cases"]:
+        if not case["ids"]:
+            continue
+        y = host(fam.gather_rows(cuda(table), cuda(np.array(case["ids"], np.int32))))
+        assert y.ravel().tolist() == case["bits"], case["cite"]
+    for case in Gt["refused"]:
+        with pytest.raises(fam.TilerCudaError) as e:
+            fam.gather_rows(cuda(table), cuda(np.array(case["ids"], np.int32)))
+        assert (e.value.position, e.value.value, e.value.extent) == (case["position"], case["value"], case["extent"])
+    p = Gt["payloads"]
+    src = np.array([h(b) for b in p["source_bits"]], np.uint32).view(np.int32)
+    y = host(fam.gather_rows(cuda(src), cuda(np.array(p["ids"], np.int32))))
+    assert y.view(np.uint32).tolist() == [h(b) for b in p["bits"]]
+
+
+@pytest.mark.parametrize("cell_id", ["w_decode_kv", "w_prefill_q", "w_prefill_mlp_in", "w_prefill_mlp_out",
+                                     "w_prefill_o", "w_vocab_slice"])
+def test_contraction_profile_digests_on_device(fam, cell_id):
+    P = G["contraction_profile_cells"]
+    cell = next(c for c in P["cells"] if c["id"] == cell_id)
+    seed = h(P["workload_seed"])
+    a = prng_values(seed, cell["m"] * cell["k"]).reshape(cell["m"], cell["k"])
+    b = prng_values(seed ^ h(P["right_seed_mask"]), cell["n"] * cell["k"]).reshape(cell["n"], cell["k"])
+    c = host(fam.contract_f32(cuda(a), cuda(b)))
+    assert hashlib.sha256(c.astype("<f4").tobytes()).hexdigest() == cell["sha256"]
+
+
+# ---- seeded parity against the oracle -----------------------------------------
+
+@pytest.mark.parametrize("rows,count", [(1, 1 << 24), (1, 1 << 20), (3, 100_003), (4, 65536), (1, 1), (2, 5000),
+                                        (7, 4096 * 3)])
+def test_grouped_sum_and_max_match_declared_grouping(fam, oracle_lib, rows, count):
+    x = seeded_uniform(11 + count, rows * count).reshape(rows, count)
+    g = fam.plan_grouping(rows, count)
+    got = host(fam.sum_f32(cuda(x), g))
+    st, want = oracle_lib.grid_fold(x, g, op=0, nthreads=8)
+    assert st == 0
+    assert_bits_equal(got, want, f"sum {g}")
+    got = host(fam.max_f32(cuda(x), g))
+    _, want = oracle_lib.grid_fold(x, g, op=1, nthreads=8)
+    assert_bits_equal(got, want, "max")
+    # the maximum is order-free: any grouping equals the strict fold
+    _, strict = oracle_lib.strict_max(x)
+    assert_bits_equal(got, strict, "max vs strict")
+
+
+def test_grouped_sum_reports_a_difference_against_the_neighbouring_grouping(fam, oracle_lib):
+    """The perturbation the reference's conformance runs demand: the kernel
+    result must differ from a neighbouring grouping's on these operands, so
+    the bit equality above is not vacuous."""
+    count = 1 << 22
+    x = (seeded_normal(5, count) * 1e4).astype(np.float32)
+    g = fam.plan_grouping(1, count)
+    got = host(fam.sum_f32(cuda(x), g))
+    _, strict = oracle_lib.strict_sum(x)
+    _, part = oracle_lib.partitioned_sum(x, 2048, count // 2048)
+    assert bits_of(got) != bits_of(strict) or bits_of(got) != bits_of(part)
+
+
+def test_explicit_groupings_including_padding_and_strict_combine(fam, oracle_lib):
+    x = seeded_normal(9, 3 * 12_000).reshape(3, 12_000)
+    for g in [dict(partitions=1, threads=64, k=1, rounds=188, combine_threads=0, combine_k=0, combine_rounds=0),
+              dict(partitions=4, threads=128, k=4, rounds=6, combine_threads=0, combine_k=0, combine_rounds=0),
+              dict(partitions=100, threads=32, k=2, rounds=2, combine_threads=64, combine_k=1, combine_rounds=2),
+              dict(partitions=3, threads=1024, k=4, rounds=1, combine_threads=32, combine_k=1, combine_rounds=1)]:
+        got = host(fam.sum_f32(cuda(x), g))
+        st, want = oracle_lib.grid_fold(x, g, op=0)
+        assert st == 0
+        assert_bits_equal(got, want, str(g))
+
+
+def test_reference_vocabulary_sums_match_the_oracle(fam, oracle_lib):
+    x = seeded_normal(3, 4 * 4096).reshape(4, 4096) * 100
+    assert_bits_equal(host(fam.strict_sum_f32(cuda(x))), oracle_lib.strict_sum(x)[1])
+    assert_bits_equal(host(fam.partitioned_sum_f32(cuda(x), 64, 64)), oracle_lib.partitioned_sum(x, 64, 64)[1])
+    for pm in (False, True):
+        assert_bits_equal(host(fam.cooperative_sum_f32(cuda(x), 32, 8, 16, pm)),
+                          oracle_lib.cooperative_sum(x, 32, 8, 16, pm)[1])
+
+
+def test_empty_sum_is_positive_zero_and_empty_max_is_refused(fam):
+    x = torch.empty((3, 0), dtype=torch.float32, device="cuda")
+    assert bits_of(host(fam.strict_sum_f32(x))) == [0, 0, 0]
+    with pytest.raises(Exception):
+        fam.max_f32(x, dict(partitions=1, threads=32, k=1, rounds=1))
+
+
+@pytest.mark.parametrize("rows,extent,full_w", [(8192, 4096, False), (300, 4096, True), (37, 1000, False),
+                                                (5, 12, True), (1, 4096, False), (129, 2048, False)])
+def test_rms_norm_f32_matches_oracle(fam, oracle_lib, rows, extent, full_w):
+    x = seeded_normal(rows * 7 + extent, rows * extent).reshape(rows, extent)
+    w = seeded_uniform(3, rows * extent if full_w else extent, 0.5, 1.5)
+    w = w.reshape(rows, extent) if full_w else w
+    got = host(fam.rms_norm(cuda(x), cuda(w)))
+    st, want = oracle_lib.rms_norm_f32(x, w, nthreads=8)
+    assert st == 0
+    assert_bits_equal(got, want, f"rms f32 {rows}x{extent}")
+
+
+@pytest.mark.parametrize("rows,extent", [(8192, 4096), (77, 4096), (9, 100)])
+def test_rms_norm_bf16_matches_oracle(fam, oracle_lib, rows, extent):
+    x = oracle_lib.f32_to_bf16(seeded_normal(rows + extent, rows * extent).reshape(rows, extent))
+    w = oracle_lib.f32_to_bf16(seeded_uniform(4, extent, 0.5, 1.5))
+    xt = cuda(x.view(np.int16)).view(torch.bfloat16)
+    wt = cuda(w.view(np.int16)).view(torch.bfloat16)
+    got = host(fam.rms_norm(xt, wt).view(torch.int16)).view(np.uint16)
+    st, want = oracle_lib.rms_norm_bf16(x, w, nthreads=8)
+    assert st == 0
+    assert (got == want).all(), f"{(got != want).sum()} bf16 mismatches"
+
+
+@pytest.mark.parametrize("rows,extent,period", [(2048, 2048, 2048), (64, 2048, 0), (33, 1000, 0), (16, 8192, 16),
+                                                (5, 6, 3)])
+def test_softmax_matches_oracle(fam, oracle_lib, rows, extent, period):
+    x = seeded_normal(rows + extent, rows * extent, std=3.0).reshape(rows, extent)
+    got = host(fam.softmax(cuda(x), causal_period=period))
+    st, want = oracle_lib.softmax_f32(x, causal_period=period, nthreads=8)
+    assert st == 0
+    assert_bits_equal(got, want, f"softmax {rows}x{extent}")
+
+
+def test_softmax_full_config_sampled_rows(fam, oracle_lib):
+    rows, extent = 65536, 2048
+    x = torch.randn(rows, extent, device="cuda", generator=torch.Generator("cuda").manual_seed(1)) * 3
+    y = host(fam.softmax(x, causal_period=2048))
+    xs = x.cpu().numpy()
+    sample = np.arange(0, rows, 509)
+    st, want = oracle_lib.softmax_f32(xs[sample], causal_period=0, nthreads=8)
+    # the oracle call above sees unmasked rows; apply the mask explicitly
+    masked = xs[sample].copy()
+    for i, r in enumerate(sample):
+        masked[i, (r % 2048) + 1:] = masked[i, (r % 2048) + 1:] + np.float32(-np.inf)
+    st, want = oracle_lib.softmax_f32(masked, nthreads=8)
+    assert_bits_equal(y[sample], want, "softmax full-config sample")
+    # size-independent property: each row's masked tail is exactly +0.0
+    assert (y[2047, :] > 0).all() and (y[0, 1:] == 0).all()
+
+
+def test_silu_random_bit_patterns_match_oracle(fam, oracle_lib):
+    rng = np.random.default_rng(17)
+    bits = rng.integers(0, 2**32, size=1 << 20, dtype=np.uint64).astype(np.uint32)
+    x = bits.view(np.float32)
+    dense = seeded_normal(2, 1 << 20, std=20.0)
+    for arr in (x, dense):
+        got = host(fam.silu(cuda(arr)))
+        _, want = oracle_lib.silu_f32(arr)
+        assert_bits_equal(got, want, "silu")
+
+
+def test_softmax_exp_band_sweep_matches_oracle(fam, oracle_lib):
+    """Every exponent band the certified exp covers: rows of x with max 0, so
+    exp(x) is evaluated on [-104, 0] densely."""
+    x = -np.linspace(0, 110, 1 << 16, dtype=np.float32).reshape(32, 2048)
+    x[:, 0] = 0
+    got = host(fam.softmax(cuda(x)))
+    _, want = oracle_lib.softmax_f32(x, nthreads=8)
+    assert_bits_equal(got, want, "exp sweep")
+
+
+def test_scale_bias_matches_oracle(fam, oracle_lib):
+    x = seeded_normal(1, 100_001)
+    a = np.float32(1.0000001)
+    b = np.float32(-3.5)
+    got = host(fam.scale_bias(cuda(x), cuda(np.array(a)), cuda(np.array(b))))
+    _, want = oracle_lib.scale_bias_f32(x, a, b)
+    assert_bits_equal(got, want)
+    a2 = seeded_normal(2, 100_001)
+    got = host(fam.scale_bias(cuda(x), cuda(a2), cuda(np.array(b))))
+    _, want = oracle_lib.scale_bias_f32(x, a2, np.array([b]))
+    assert_bits_equal(got, want)
+
+
+@pytest.mark.parametrize("rows,extent", [(16384, 4096), (3, 1001)])
+def test_quantize_decode_match_oracle(fam, oracle_lib, rows, extent):
+    x = seeded_normal(rows, rows * extent).reshape(rows, extent)
+    codes, scales = fam.quantize_i8_rows(cuda(x))
+    st, wc, ws, _ = oracle_lib.quantize_i8_rows(x, nthreads=8)
+    assert st == 0
+    assert (host(codes) == wc).all()
+    assert_bits_equal(host(scales), ws)
+    y = host(fam.dequantize_i8_rows(codes, scales))
+    _, wy = oracle_lib.dequantize_i8_rows(wc, ws, nthreads=8)
+    assert_bits_equal(y, wy)
+
+
+def test_quantize_half_integer_ties_are_exact(fam, oracle_lib):
+    # rows whose quotients land on k + 0.5 exactly and within an ulp of it
+    s = np.float32(127.0) / np.float32(127.0)
+    row = np.array([127.0, 0.5, 1.5, 2.5, -0.5, -1.5, 63.5, np.nextafter(np.float32(2.5), np.float32(3)),
+                    np.nextafter(np.float32(2.5), np.float32(2))], np.float32)
+    x = np.tile(row, (4, 1)) * np.array([[1.0], [0.5], [3.0], [1e-3]], np.float32)
+    codes, scales = fam.quantize_i8_rows(cuda(x))
+    st, wc, ws, _ = oracle_lib.quantize_i8_rows(x)
+    assert (host(codes) == wc).all() and s == 1
+
+
+def test_quantize_refusals(fam):
+    x = np.ones((3, 8), np.float32)
+    x[1, 5] = np.nan
+    with pytest.raises(fam.TilerCudaError) as e:
+        fam.quantize_i8_rows(cuda(x))
+    assert e.value.code == 4 and e.value.position == 13
+    with pytest.raises(fam.TilerCudaError) as e:
+        fam.quantize_i8_rows(cuda(np.zeros((2, 8), np.float32)))
+    assert e.value.code == 9 and e.value.position == 0
+
+
+def test_gather_full_config_is_bit_exact(fam):
+    gen = torch.Generator("cuda").manual_seed(3)
+    table = (torch.randn(128256, 4096, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    ids = torch.randint(0, 128256, (8192,), device="cuda", dtype=torch.int32, generator=gen)
+    got = fam.gather_rows(table, ids)
+    want = table.index_select(0, ids.long())
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    bad = ids.clone()
+    bad[4000] = -7
+    bad[5000] = 128256
+    with pytest.raises(fam.TilerCudaError) as e:
+        fam.gather_rows(table, bad)
+    assert (e.value.position, e.value.value, e.value.extent) == (4000, -7, 128256)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 1024), (384, 768, 512)])
+def test_gemm_bf16_silu_matches_oracle(fam, oracle_lib, m, n, k):
+    a = oracle_lib.f32_to_bf16(seeded_normal(m + k, m * k).reshape(m, k))
+    b = oracle_lib.f32_to_bf16(seeded_normal(n + k, n * k).reshape(n, k) * 0.05)
+    at = cuda(a.view(np.int16)).view(torch.bfloat16)
+    bt = cuda(b.view(np.int16)).view(torch.bfloat16)
+    for epi in ("none", "silu"):
+        got = oracle_lib.bf16_to_f32(host(fam.gemm_bf16(at, bt, epilogue=epi).view(torch.int16)).view(np.uint16))
+        st, want = oracle_lib.gemm_bf16_silu(a, b, apply_silu=(epi == "silu"), nthreads=8)
+        want = oracle_lib.bf16_to_f32(want)
+        err = np.abs(got - want) / np.maximum(np.abs(want), 1e-2)
+        assert err.max() <= 1e-2, f"{epi}: max rel err {err.max()}"
+
+
+def test_gemm_bf16_full_config_sampled_rows(fam, oracle_lib):
+    m, n, k = 8192, 14336, 4096
+    gen = torch.Generator("cuda").manual_seed(5)
+    a = (torch.randn(m, k, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, k, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+    c = fam.gemm_bf16(a, b, epilogue="silu")
+    rows = [0, 1, 127, 128, 4095, 8191]
+    an = a.view(torch.int16).cpu().numpy().view(np.uint16)
+    bn = b.view(torch.int16).cpu().numpy().view(np.uint16)
+    got = oracle_lib.bf16_to_f32(c.view(torch.int16).cpu().numpy().view(np.uint16)[rows])
+    want = np.stack([oracle_lib.bf16_to_f32(oracle_lib.gemm_bf16_silu(an, bn, r, r + 1, nthreads=8)[1])[0]
+                     for r in rows])
+    err = np.abs(got - want) / np.maximum(np.abs(want), 1e-3)
+    assert err.max() <= 1e-2, f"max rel err {err.max()}"

@@ -1,0 +1,373 @@
+// Shared device numerics and PTX helpers for the tiler-cuda kernels (sm_100a).
+//
+// Numerical rules restated from moderately-ai/tiler's tiler-reference:
+//  * every binary32 + - * / is one IEEE RNE operation, subnormals preserved
+//    (the library is built with -fmad=false and without -ftz / fast-math, and
+//    the kernels spell the reference's separate roundings with __fadd_rn /
+//    __fmul_rn / __fdiv_rn so no contraction can fuse them);
+//  * arithmetic NaN results are canonicalized to 0x7fc00000
+//    (crates/tiler-reference/src/lib.rs:144-150);
+//  * exp and 1/sqrt are correctly rounded (certified) binary32 values
+//    (silu.rs:220-277, rms_norm.rs:238-293).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tiler_cuda.h"
+
+namespace tc {
+
+constexpr uint32_t kCanonicalNan = 0x7fc00000u;
+
+__host__ __device__ __forceinline__ uint64_t umin64(uint64_t a, uint64_t b) { return a < b ? a : b; }
+
+__device__ __forceinline__ float canon(float v) {
+  return isnan(v) ? __uint_as_float(kCanonicalNan) : v;
+}
+
+// maximum_f32 — crates/tiler-reference/src/softmax.rs:168-186.
+__device__ __forceinline__ float maximum(float a, float b) {
+  if (isnan(a) || isnan(b)) return __uint_as_float(kCanonicalNan);
+  if (a == b) return __uint_as_float(__float_as_uint(a) & __float_as_uint(b));
+  return a > b ? a : b;
+}
+
+// Bf16 RNE rounding of a binary32 value, canonical NaN 0x7fc0
+// (crates/tiler-reference/src/bf16.rs:393-580).
+__device__ __forceinline__ uint16_t f32_to_bf16(float v) {
+  if (isnan(v)) return 0x7fc0;
+  uint32_t b = __float_as_uint(v);
+  b += 0x7fffu + ((b >> 16) & 1u);
+  return (uint16_t)(b >> 16);
+}
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// ---- device status word --------------------------------------------------
+
+// error_key = (position << 8) | code; the smallest position wins.
+__device__ __forceinline__ void report_error(tiler_cuda_status* s, uint64_t position, uint32_t code) {
+  if (s) atomicMin((unsigned long long*)&s->error_key, (unsigned long long)((position << 8) | code));
+}
+__device__ __forceinline__ void report_value(tiler_cuda_status* s, uint64_t position, uint32_t value) {
+  if (s) atomicMin((unsigned long long*)&s->value_key, (unsigned long long)((position << 32) | value));
+}
+__device__ __forceinline__ void report_undecided(tiler_cuda_status* s) {
+  if (s) atomicAdd(&s->undecided, 1u);
+}
+
+// ---- correctly rounded exp --------------------------------------------------
+//
+// Tang's table-driven method (P. T. P. Tang, "Table-driven implementation of
+// the exponential function in IEEE floating-point arithmetic", ACM TOMS 15(2),
+// 1989) carried out in binary64 and rounded once to binary32, then certified:
+//   x = (256 m + j) ln2/256 + r,  |r| <= ln2/512,
+//   e^x = 2^m * 2^(j/256) * e^r,  e^r - 1 by its Taylor polynomial.
+// The binary64 value carries a relative error below 2^-51; it is accepted
+// only when it lies farther than 2^-49 (relative) from every binary32
+// rounding midpoint.  Otherwise the rare slow path re-evaluates in
+// double-double (error below 2^-100) and decides against the midpoints; a
+// value still undecided there is counted in the status word, mirroring the
+// reference's UndecidedTranscendentalReference refusal.
+//
+// The 2^(j/256) table (hi + lo doubles) is written once per device by the
+// host runtime (runtime.cu, from __float128 exp2q) into g_exp2_table; the fast
+// path reads its hi column from a shared-memory copy.
+
+__device__ double g_exp2_table[256][2];
+
+// 256/ln2 and ln2/256 split so that n*kLn2By256Hi is exact for |n| < 2^17.
+constexpr double kInvLn2x256 = 369.3299304675746271;            // 256 / ln 2 (rounded)
+constexpr double kLn2By256Hi = 0x1.62e42fefa0000p-9;             // 36 significant bits
+constexpr double kLn2By256Mid = 0x1.cf79abc9e3b3ap-48;           // next 53 bits
+constexpr double kLn2By256Lo = -0x1.ff0342542fc33p-102;           // remainder
+
+__device__ __forceinline__ double pow2_double(int m) {  // 2^m for -1022 <= m <= 1023
+  return __longlong_as_double((long long)(m + 1023) << 52);
+}
+
+__device__ __forceinline__ float next_up(float f) {  // f >= 0 finite
+  return f == 0.0f ? __uint_as_float(1u) : __uint_as_float(__float_as_uint(f) + 1u);
+}
+__device__ __forceinline__ float next_down(float f) {  // f > 0
+  return __uint_as_float(__float_as_uint(f) - 1u);
+}
+
+// Midpoint between the largest finite binary32 and 2^128: everything at or
+// above it rounds to +inf (silu.rs:246-249).
+constexpr double kOverflowMidpoint = 340282356779733661637539395458142568448.0;  // 2^128 - 2^103
+
+// Distance test of a positive binary64 approximation y (relative error bound
+// tol) against the midpoints around f = rn32(y).  Returns true when decided.
+__device__ __forceinline__ bool decided(double y, float f, double tol) {
+  double t = tol * y;
+  if (isinf(f)) return y - t > kOverflowMidpoint;
+  double fd = f;
+  double upper = (__float_as_uint(f) == 0x7f7fffffu) ? kOverflowMidpoint : 0.5 * (fd + (double)next_up(f));
+  if (y + t >= upper) return false;
+  if (f == 0.0f) return true;  // nothing below zero is reachable
+  double lower = 0.5 * (fd + (double)next_down(f));
+  return y - t > lower;
+}
+
+// Double-double helpers (Dekker / Knuth error-free transformations).
+struct dd { double hi, lo; };
+__device__ __forceinline__ dd two_sum(double a, double b) {
+  double s = __dadd_rn(a, b);
+  double bb = __dsub_rn(s, a);
+  double e = __dadd_rn(__dsub_rn(a, __dsub_rn(s, bb)), __dsub_rn(b, bb));
+  return {s, e};
+}
+__device__ __forceinline__ dd two_prod(double a, double b) {
+  double p = __dmul_rn(a, b);
+  return {p, __fma_rn(a, b, -p)};
+}
+__device__ __forceinline__ dd dd_add(dd a, dd b) {
+  dd s = two_sum(a.hi, b.hi);
+  double e = __dadd_rn(s.lo, __dadd_rn(a.lo, b.lo));
+  return two_sum(s.hi, e);
+}
+__device__ __forceinline__ dd dd_mul(dd a, dd b) {
+  dd p = two_prod(a.hi, b.hi);
+  double e = __fma_rn(a.hi, b.lo, __fma_rn(a.lo, b.hi, p.lo));
+  return two_sum(p.hi, e);
+}
+__device__ __forceinline__ dd dd_mul_d(dd a, double b) {
+  dd p = two_prod(a.hi, b);
+  return two_sum(p.hi, __fma_rn(a.lo, b, p.lo));
+}
+
+// Rounds the double-double Y = y.hi + y.lo (> 0, relative error <= 2^-100)
+// to binary32, deciding against the midpoints; flags when it cannot decide.
+__device__ __noinline__ float round_dd_to_f32(dd y, bool* undecided) {
+  float f = __double2float_rn(y.hi);
+  const double tol = 0x1p-98 * y.hi;
+  if (isinf(f)) {
+    double d = __dadd_rn(__dsub_rn(y.hi, kOverflowMidpoint), y.lo);
+    if (fabs(d) <= tol) *undecided = true;
+    return d > 0 ? f : 3.40282347e38f;
+  }
+  double fd = f;
+  if (__float_as_uint(f) != 0x7f7fffffu) {
+    double upper = 0.5 * (fd + (double)next_up(f));
+    double du = __dadd_rn(__dsub_rn(y.hi, upper), y.lo);
+    if (fabs(du) <= tol) *undecided = true;
+    if (du > 0) return next_up(f);
+  }
+  if (f != 0.0f) {
+    double lower = 0.5 * (fd + (double)next_down(f));
+    double dl = __dadd_rn(__dsub_rn(y.hi, lower), y.lo);
+    if (fabs(dl) <= tol) *undecided = true;
+    if (dl < 0) return next_down(f);
+  }
+  return f;
+}
+
+// Slow path: e^x in double-double.
+__device__ __noinline__ float exp_slow(float x, int n, bool* undecided) {
+  double nd = (double)n;
+  // r = x - n ln2/256 as a double-double: x - n*Hi is exact (Sterbenz).
+  double r0 = __fma_rn(-nd, kLn2By256Hi, (double)x);
+  dd nm = two_prod(nd, kLn2By256Mid);
+  dd r = two_sum(r0, -nm.hi);
+  r.lo = __dsub_rn(__dsub_rn(r.lo, nm.lo), nd * kLn2By256Lo);
+  r = two_sum(r.hi, r.lo);
+  // e^r - 1 = sum_{i=1..10} r^i / i!, terms formed in double-double
+  // (|r| <= 2^-9.4, so the first omitted term is below 2^-110).
+  dd term = r, em1 = r;
+  for (int i = 2; i <= 10; ++i) {
+    term = dd_mul(term, r);
+    double q = term.hi / (double)i;
+    dd qi = two_prod(q, (double)i);
+    double rem = __dadd_rn(__dsub_rn(term.hi, qi.hi), __dsub_rn(term.lo, qi.lo));
+    term = two_sum(q, rem / (double)i);
+    em1 = dd_add(em1, term);
+  }
+  int j = n & 255, m = n >> 8;
+  dd t = {g_exp2_table[j][0], g_exp2_table[j][1]};
+  dd y = dd_add(t, dd_mul(t, em1));
+  // scale by 2^m in two exact steps (m >= -152, and y.hi*2^m stays normal)
+  double s = pow2_double(m);
+  y.hi *= s;
+  y.lo *= s;
+  return round_dd_to_f32(y, undecided);
+}
+
+// Correctly rounded binary32 e^x (certified_exp_strict, silu.rs:220-277).
+// `table_hi` is a shared-memory (or global) copy of g_exp2_table[.][0].
+__device__ __forceinline__ float exp_cr(float x, const double* table_hi, tiler_cuda_status* st) {
+  if (isnan(x)) return __uint_as_float(kCanonicalNan);
+  if (x >= 89.0f) return __uint_as_float(0x7f800000u);
+  if (x <= -104.0f) return 0.0f;
+  if (x == 0.0f) return 1.0f;
+  double xd = (double)x;
+  double nd = rint(xd * kInvLn2x256);
+  int n = (int)nd;
+  double r = __fma_rn(-nd, kLn2By256Hi, xd);  // exact
+  r = __fma_rn(-nd, kLn2By256Mid, r);
+  // e^r - 1 ~ r + r^2 (1/2 + r (1/6 + r/24)); |r| <= 2^-9.4, remainder < 2^-56
+  double q = __fma_rn(r, 1.0 / 24.0, 1.0 / 6.0);
+  q = __fma_rn(r, q, 0.5);
+  double p = __fma_rn(__dmul_rn(r, r), q, r);
+  int j = n & 255, m = n >> 8;
+  double t = table_hi[j];
+  double y = __fma_rn(t, p, t) * pow2_double(m);
+  float f = __double2float_rn(y);
+  if (decided(y, f, 0x1p-49)) return f;
+  bool und = false;
+  f = exp_slow(x, n, &und);
+  if (und) report_undecided(st);
+  return f;
+}
+
+// Correctly rounded binary32 1/sqrt(t) (certified_rsqrt_strict,
+// rms_norm.rs:238-293).  The binary64 candidate is checked exactly: f is the
+// correctly rounded value iff mlo^2 t < 1 < mhi^2 t for the midpoints mlo,
+// mhi around f; m^2 is exact in binary64 (25-bit m) and m^2 t is formed
+// exactly as a double-double.
+__device__ __forceinline__ int cmp_sq_times_one(double m, float t) {
+  double m2 = m * m;  // exact
+  double ph = m2 * (double)t;
+  double pl = __fma_rn(m2, (double)t, -ph);
+  if (ph > 1.0) return 1;
+  if (ph < 1.0) return -1;
+  return pl > 0 ? 1 : (pl < 0 ? -1 : 0);
+}
+
+__device__ __forceinline__ float rsqrt_cr(float t) {
+  if (isnan(t)) return __uint_as_float(kCanonicalNan);
+  if (isinf(t)) return t > 0 ? 0.0f : __uint_as_float(kCanonicalNan);
+  if (t == 0.0f) return signbit(t) ? __uint_as_float(0xff800000u) : __uint_as_float(0x7f800000u);
+  if (t < 0.0f) return __uint_as_float(kCanonicalNan);
+  float f = __double2float_rn(__drcp_rn(__dsqrt_rn((double)t)));
+  for (int it = 0; it < 4; ++it) {
+    double fd = f;
+    double mhi = 0.5 * (fd + (double)next_up(f));
+    if (cmp_sq_times_one(mhi, t) <= 0) { f = next_up(f); continue; }  // root >= mhi
+    double mlo = 0.5 * (fd + (double)next_down(f));
+    if (cmp_sq_times_one(mlo, t) >= 0) { f = next_down(f); continue; }  // root <= mlo
+    break;
+  }
+  return f;
+}
+
+// SiLU — silu_f32_under, crates/tiler-reference/src/silu.rs:158-180.
+__device__ __forceinline__ float silu_cr(float x, const double* table_hi, tiler_cuda_status* st) {
+  if (isnan(x)) return __uint_as_float(kCanonicalNan);
+  if (isinf(x)) return x > 0 ? x : __uint_as_float(kCanonicalNan);
+  float e = exp_cr(-x, table_hi, st);
+  float d = __fadd_rn(1.0f, e);
+  return canon(__fdiv_rn(x, d));
+}
+
+// Copies the 2^(j/256) hi column into shared memory (call by all threads,
+// followed by __syncthreads()).
+__device__ __forceinline__ void load_exp_table(double* smem_table) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) smem_table[i] = g_exp2_table[i][0];
+}
+
+// ---- PTX wrappers: mbarrier, bulk copies, TMA ---------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}" ::"r"(smem_u32(bar)),
+               "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: polls the barrier phase and gives up after about two seconds
+// of %globaltimer time, recording a timeout in the status word instead of
+// hanging the device.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, tiler_cuda_status* st) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+  }
+  if (st) atomicAdd(&st->timeouts, 1u);
+  return false;
+}
+
+// 1D bulk copy global -> shared, completing on an mbarrier (16-byte aligned
+// addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// 2D tiled TMA load (no multicast) completing on an mbarrier.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, int32_t x, int32_t y, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ float4 ld_global_policy(const float4* p, uint64_t policy) {
+  float4 v;
+  asm volatile("ld.global.L2::cache_hint.v4.f32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p), "l"(policy));
+  return v;
+}
+__device__ __forceinline__ void st_global_stream(float4* p, float4 v) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_global_nc_u4(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_global_stream_u4(uint4* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+}  // namespace tc

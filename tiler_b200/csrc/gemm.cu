@@ -1,0 +1,289 @@
+// Contraction family.
+//
+//  * contract_f32: the reference-exact `td,od->to` f32 contraction
+//    (contraction.rs:558-630): every output is a strict fold over k in
+//    ascending order, seeded at the first product, product and sum rounded
+//    separately.  16x16 output tiles stage 32-wide k slabs of A and B in
+//    shared memory; each thread still folds its own output in k order.
+//
+//  * gemm_bf16: the config's bf16 contraction on the 5th-generation tensor
+//    cores.  A persistent kernel, one CTA per SM, 128x256 output tiles:
+//      warp 0     TMA producer: 128x64 A and 256x64 B bf16 boxes, 128-byte
+//                 swizzle, into a 4-stage shared-memory ring (no multicast);
+//      warp 1     allocates 512 TMEM columns (two 128x256 f32 accumulators)
+//                 and one lane issues tcgen05.mma (kind::f16, M=128, N=256,
+//                 K=16) and tcgen05.commit back to the ring / accumulators;
+//      warps 2-5  epilogue: tcgen05.ld 32 columns at a time, the SiLU of
+//                 silu.rs:158-180 (certified exp), RNE to bf16, 16-byte
+//                 stores; accumulator b of tile i+1 fills while tile i drains.
+//    Every mbarrier wait is bounded; a wait that gives up records a timeout
+//    in the status word and the CTA stops, frees its TMEM and returns.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tc {
+
+// ---------------------------------------------------------------------------
+// Strict f32 contraction
+// ---------------------------------------------------------------------------
+__global__ void contract_f32_kernel(const float* __restrict__ a, const float* __restrict__ b, uint64_t m,
+                                    uint64_t n, uint64_t k, float* __restrict__ c) {
+  __shared__ float As[16][33], Bs[16][33];
+  const uint32_t tx = threadIdx.x, ty = threadIdx.y;
+  const uint64_t row = blockIdx.y * 16ull + ty, col = blockIdx.x * 16ull + tx;
+  const uint64_t arow = blockIdx.y * 16ull + ty, brow = blockIdx.x * 16ull + ty;
+  float acc = 0.0f;
+  for (uint64_t k0 = 0; k0 < k; k0 += 32) {
+    for (uint32_t kk = tx; kk < 32; kk += 16) {
+      As[ty][kk] = (arow < m && k0 + kk < k) ? a[arow * k + k0 + kk] : 0.0f;
+      Bs[ty][kk] = (brow < n && k0 + kk < k) ? b[brow * k + k0 + kk] : 0.0f;
+    }
+    __syncthreads();
+    const uint32_t lim = (uint32_t)umin64(32, k - k0);
+    for (uint32_t kk = 0; kk < lim; ++kk) {
+      const float p = canon(__fmul_rn(As[ty][kk], Bs[tx][kk]));
+      acc = (k0 == 0 && kk == 0) ? p : canon(__fadd_rn(acc, p));
+    }
+    __syncthreads();
+  }
+  if (row < m && col < n) c[row * n + col] = canon(acc);
+}
+
+void launch_contract_f32(const float* a, const float* b, uint64_t m, uint64_t n, uint64_t k, float* c,
+                         cudaStream_t stream) {
+  dim3 block(16, 16), grid((unsigned)((n + 15) / 16), (unsigned)((m + 15) / 16));
+  contract_f32_kernel<<<grid, block, 0, stream>>>(a, b, m, n, k, c);
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 bf16 GEMM
+// ---------------------------------------------------------------------------
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kTileABytes = kBM * kBK * 2;  // 16 KB
+constexpr int kTileBBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kStageBytes = kTileABytes + kTileBBytes;
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+
+struct GemmBars {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + 2048 /*exp table*/ +
+                             sizeof(GemmBars) + 64;
+
+// Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): K-major,
+// 128-byte swizzle, 8-row core groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3fff);        // start address
+  d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset
+  d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                         // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::f16, A/B bf16, D f32, both K-major, M=128, N=256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+#define TMEM_LD32(taddr, r)                                                                                         \
+  asm volatile(                                                                                                     \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19," \
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                                    \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),           \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),     \
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),   \
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])    \
+      : "r"(taddr))
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                             uint32_t m_blocks, uint32_t n_blocks, uint32_t k_blocks, int epilogue,
+                             uint16_t* __restrict__ c, uint64_t ldc, tiler_cuda_status* st) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = ((raw + 1023) & ~1023u) - raw;
+  uint8_t* tiles = smem_raw + pad;
+  double* table = reinterpret_cast<double*>(tiles + (size_t)kStages * kStageBytes);
+  GemmBars& B = *reinterpret_cast<GemmBars*>(tiles + (size_t)kStages * kStageBytes + 2048);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t num_tiles = m_blocks * n_blocks;
+
+  load_exp_table(table);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) { mbar_init(&B.full[s], 1); mbar_init(&B.empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&B.tmem_full[s], 1); mbar_init(&B.tmem_empty[s], 128); }
+    B.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem_base = B.tmem_base;
+  volatile int* abort_flag = &B.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      uint64_t it = 0;
+      for (uint32_t tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        const uint32_t mb = tile % m_blocks, nb = tile / m_blocks;
+        for (uint32_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          const uint64_t use = it / kStages;
+          if (use > 0 && !mbar_wait(&B.empty[s], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
+          uint8_t* sa = tiles + (size_t)s * kStageBytes;
+          mbar_arrive_expect_tx(&B.full[s], kStageBytes);
+          tma_load_2d(sa, &tmap_a, (int)(kb * kBK), (int)(mb * kBM), &B.full[s], keep);
+          tma_load_2d(sa + kTileABytes, &tmap_b, (int)(kb * kBK), (int)(nb * kBN), &B.full[s], keep);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint64_t it = 0;
+      uint32_t local = 0;
+      for (uint32_t tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
+        const uint32_t buf = local & 1;
+        const uint32_t use = local >> 1;
+        if (use > 0 && !mbar_wait(&B.tmem_empty[buf], (use - 1) & 1, st)) { *abort_flag = 1; break; }
+        tmem_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * kBN;
+        for (uint32_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (!mbar_wait(&B.full[s], (uint32_t)((it / kStages) & 1), st)) { *abort_flag = 1; break; }
+          tmem_fence_after();
+          const uint32_t sa = smem_u32(tiles + (size_t)s * kStageBytes);
+          const uint32_t sb = sa + kTileABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16(d_tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), (kb | kk) != 0);
+          mma_commit(&B.empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (*abort_flag) break;
+        mma_commit(&B.tmem_full[buf]);  // the accumulator is complete
+      }
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quarter (warp % 4)
+    const uint32_t quarter = warp & 3;
+    const uint32_t row_in_tile = quarter * 32 + lane;
+    uint32_t local = 0;
+    for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const uint32_t mb = tile % m_blocks, nb = tile / m_blocks;
+      const uint32_t buf = local & 1;
+      if (!mbar_wait(&B.tmem_full[buf], (local >> 1) & 1, st)) { *abort_flag = 1; break; }
+      if (*abort_flag) break;
+      tmem_fence_after();
+      const uint64_t row = (uint64_t)mb * kBM + row_in_tile;
+      uint16_t* crow = c + row * ldc + (uint64_t)nb * kBN;
+#pragma unroll 1
+      for (uint32_t col = 0; col < (uint32_t)kBN; col += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + buf * kBN + col;
+        TMEM_LD32(taddr, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
+          if (epilogue == 1) {
+            v0 = silu_cr(v0, table, st);
+            v1 = silu_cr(v1, table, st);
+          } else {
+            v0 = canon(v0);
+            v1 = canon(v1);
+          }
+          packed[j] = (uint32_t)f32_to_bf16(v0) | ((uint32_t)f32_to_bf16(v1) << 16);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+      }
+      tmem_fence_before();
+      mbar_arrive(&B.tmem_empty[buf]);
+    }
+  }
+  tmem_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// K-major bf16 matrix [rows, k] -> tensor map with a (64 x box_rows) box.
+static bool make_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {k * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k, int epilogue,
+                     uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  if (m % kBM || n % kBN || k % kBK || k == 0) return TILER_CUDA_UNSUPPORTED;
+  if ((uintptr_t)a % 16 || (uintptr_t)b % 16 || (uintptr_t)c % 16 || ldc % 8 || ldc < n) return TILER_CUDA_UNSUPPORTED;
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, a, m, k, kBM) || !make_tmap(&tb, b, n, k, kBN)) return TILER_CUDA_DEVICE_ERROR;
+  const uint32_t mbk = (uint32_t)(m / kBM), nbk = (uint32_t)(n / kBN), kbk = (uint32_t)(k / kBK);
+  const uint32_t tiles = mbk * nbk;
+  const unsigned grid = std::min<uint32_t>(tiles, (uint32_t)sm_count);
+  cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
+  gemm_bf16_tcgen05_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(ta, tb, mbk, nbk, kbk, epilogue, c, ldc, st);
+  return TILER_CUDA_OK;
+}
+
+}  // namespace tc

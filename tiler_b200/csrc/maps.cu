@@ -1,0 +1,184 @@
+// Elementwise maps (SiLU, scale-bias), the row gather, the reference's own
+// per-tensor unsigned strict-affine quantize / decode, and the status-word
+// reset.  All are grid-stride kernels sized to a multiple of the SM count,
+// with 16-byte vector access where the pointers allow.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tc {
+
+__global__ void status_reset_kernel(tiler_cuda_status* st) {
+  st->error_key = ~0ull;
+  st->value_key = ~0ull;
+  st->undecided = 0;
+  st->timeouts = 0;
+  st->reserved = 0;
+}
+
+void launch_status_reset(tiler_cuda_status* st, cudaStream_t stream) { status_reset_kernel<<<1, 1, 0, stream>>>(st); }
+
+// SiluF32Reference — silu.rs:78-110 (map) and :158-180 (scalar).
+__global__ void silu_kernel(const float* __restrict__ x, uint64_t n, float* __restrict__ y, tiler_cuda_status* st) {
+  __shared__ double table[256];
+  load_exp_table(table);
+  __syncthreads();
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0)) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    for (uint64_t v = tid; v < n / 4; v += stride) {
+      float4 q = __ldcs(x4 + v);
+      q.x = silu_cr(q.x, table, st);
+      q.y = silu_cr(q.y, table, st);
+      q.z = silu_cr(q.z, table, st);
+      q.w = silu_cr(q.w, table, st);
+      st_global_stream(y4 + v, q);
+    }
+    for (uint64_t i = n / 4 * 4 + tid; i < n; i += stride) y[i] = silu_cr(x[i], table, st);
+  } else {
+    for (uint64_t i = tid; i < n; i += stride) y[i] = silu_cr(x[i], table, st);
+  }
+}
+
+void launch_silu(const float* x, uint64_t n, float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  if (n == 0) return;
+  const uint64_t want = (n / 4 + 255) / 256 + 1;
+  silu_kernel<<<(unsigned)std::min<uint64_t>(want, (uint64_t)sm_count * 8), 256, 0, stream>>>(x, n, y, st);
+}
+
+// multiply-f32 then add-f32, two roundings (standard.rs:105-120,
+// evaluate.rs:448-485), NaN canonicalized after each operation.
+__device__ __forceinline__ float scale_bias1(float x, float a, float b) {
+  return canon(__fadd_rn(canon(__fmul_rn(x, a)), b));
+}
+
+__global__ void scale_bias_kernel(const float* __restrict__ x, uint64_t n, const float* __restrict__ a, int a_scalar,
+                                  const float* __restrict__ b, int b_scalar, float* __restrict__ y) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t tid = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  const bool vec = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && (a_scalar || (uintptr_t)a % 16 == 0) &&
+                   (b_scalar || (uintptr_t)b % 16 == 0);
+  const float as = a_scalar ? __ldg(a) : 0.0f, bs = b_scalar ? __ldg(b) : 0.0f;
+  uint64_t done = 0;
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    for (uint64_t v = tid; v < n / 4; v += stride) {
+      const float4 q = __ldcs(x4 + v);
+      const float4 av = a_scalar ? make_float4(as, as, as, as) : __ldcs(reinterpret_cast<const float4*>(a) + v);
+      const float4 bv = b_scalar ? make_float4(bs, bs, bs, bs) : __ldcs(reinterpret_cast<const float4*>(b) + v);
+      st_global_stream(y4 + v, make_float4(scale_bias1(q.x, av.x, bv.x), scale_bias1(q.y, av.y, bv.y),
+                                           scale_bias1(q.z, av.z, bv.z), scale_bias1(q.w, av.w, bv.w)));
+    }
+    done = n / 4 * 4;
+  }
+  for (uint64_t i = done + tid; i < n; i += stride)
+    y[i] = scale_bias1(x[i], a_scalar ? as : a[i], b_scalar ? bs : b[i]);
+}
+
+void launch_scale_bias(const float* x, uint64_t n, const float* a, int a_scalar, const float* b, int b_scalar,
+                       float* y, int sm_count, cudaStream_t stream) {
+  if (n == 0) return;
+  const uint64_t want = (n / 4 + 255) / 256 + 1;
+  scale_bias_kernel<<<(unsigned)std::min<uint64_t>(want, (uint64_t)sm_count * 8), 256, 0, stream>>>(
+      x, n, a, a_scalar, b, b_scalar, y);
+}
+
+// GatherF32Reference (structural.rs:513-606): bit-exact row copies; an
+// out-of-range id is reported with its position and value (the smallest
+// position wins, as the reference refuses at the first one in order) and
+// its row is not written.
+__global__ void gather_rows_kernel(const uint8_t* __restrict__ table, uint64_t table_rows, uint64_t row_bytes,
+                                   const void* __restrict__ ids, int ids_unsigned, uint64_t n_ids,
+                                   uint8_t* __restrict__ out, tiler_cuda_status* st) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  const bool vec = (row_bytes % 16 == 0) && ((uintptr_t)table % 16 == 0) && ((uintptr_t)out % 16 == 0);
+  for (uint64_t i = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32; i < n_ids; i += warps) {
+    int64_t v = ids_unsigned ? (int64_t)__ldg((const uint32_t*)ids + i) : (int64_t)__ldg((const int32_t*)ids + i);
+    if (v < 0 || (uint64_t)v >= table_rows) {
+      if (lane == 0) {
+        report_error(st, i, TILER_CUDA_GATHER_INDEX_OUT_OF_BOUNDS);
+        report_value(st, i, (uint32_t)v);
+      }
+      continue;
+    }
+    const uint8_t* src = table + (uint64_t)v * row_bytes;
+    uint8_t* dst = out + i * row_bytes;
+    if (vec) {
+      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      const uint64_t nv = row_bytes / 16;
+      uint64_t k = lane;
+      for (; k + 32 * 3 < nv; k += 32 * 4) {
+        const uint4 a0 = ld_global_nc_u4(s4 + k), a1 = ld_global_nc_u4(s4 + k + 32);
+        const uint4 a2 = ld_global_nc_u4(s4 + k + 64), a3 = ld_global_nc_u4(s4 + k + 96);
+        st_global_stream_u4(d4 + k, a0);
+        st_global_stream_u4(d4 + k + 32, a1);
+        st_global_stream_u4(d4 + k + 64, a2);
+        st_global_stream_u4(d4 + k + 96, a3);
+      }
+      for (; k < nv; k += 32) st_global_stream_u4(d4 + k, ld_global_nc_u4(s4 + k));
+    } else {
+      for (uint64_t k = lane; k < row_bytes; k += 32) dst[k] = src[k];
+    }
+  }
+}
+
+void launch_gather_rows(const void* table, uint64_t table_rows, uint64_t row_bytes, const void* ids,
+                        int ids_unsigned, uint64_t n_ids, void* out, tiler_cuda_status* st, int sm_count,
+                        cudaStream_t stream) {
+  if (n_ids == 0 || row_bytes == 0) return;
+  const unsigned wpb = 8;
+  const uint64_t want = (n_ids + wpb - 1) / wpb;
+  gather_rows_kernel<<<(unsigned)std::min<uint64_t>(want, (uint64_t)sm_count * 16), wpb * 32, 0, stream>>>(
+      (const uint8_t*)table, table_rows, row_bytes, ids, ids_unsigned, n_ids, (uint8_t*)out, st);
+}
+
+// quantize_one / dequantize_one — quantization.rs:404-451 (per-tensor scale,
+// unsigned codes, maximum 15 or 255).
+__global__ void quantize_affine_u8_kernel(const float* __restrict__ x, uint64_t n, float scale, uint32_t zp,
+                                          uint32_t maximum, uint8_t* __restrict__ codes, tiler_cuda_status* st) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const float v = x[i];
+    if (isnan(v)) {
+      report_error(st, i, TILER_CUDA_NAN_INPUT);
+      continue;
+    }
+    const float s = __fdiv_rn(v, scale);
+    const float t = __fadd_rn(s, (float)zp);
+    const float c = fminf(fmaxf(t, 0.0f), (float)maximum);
+    codes[i] = (uint8_t)__float2uint_rn(c);
+  }
+}
+
+__global__ void dequantize_affine_u8_kernel(const uint8_t* __restrict__ codes, uint64_t n, float scale, uint32_t zp,
+                                            uint32_t maximum, float* __restrict__ y, tiler_cuda_status* st) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const uint32_t c = codes[i];
+    if (c > maximum) {  // the code domain check of dense_code_bytes (quantization.rs:308-327)
+      report_error(st, i, TILER_CUDA_INVALID_APPLICATION);
+      continue;
+    }
+    y[i] = c == zp ? 0.0f : __fmul_rn((float)((int32_t)c - (int32_t)zp), scale);
+  }
+}
+
+void launch_quantize_affine_u8(const float* x, uint64_t n, float scale, uint32_t zp, uint32_t maximum,
+                               uint8_t* codes, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  if (n == 0) return;
+  quantize_affine_u8_kernel<<<(unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)sm_count * 8), 256, 0,
+                              stream>>>(x, n, scale, zp, maximum, codes, st);
+}
+
+void launch_dequantize_affine_u8(const uint8_t* codes, uint64_t n, float scale, uint32_t zp, uint32_t maximum,
+                                 float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  if (n == 0) return;
+  dequantize_affine_u8_kernel<<<(unsigned)std::min<uint64_t>((n + 255) / 256, (uint64_t)sm_count * 8), 256, 0,
+                                stream>>>(codes, n, scale, zp, maximum, y, st);
+}
+
+}  // namespace tc

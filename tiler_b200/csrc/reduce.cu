@@ -1,0 +1,276 @@
+// Reduction families: the grouped fold (sum / governed maximum) under the
+// backend's declared grouping, plus the reference-vocabulary groupings
+// (strict serial, strict partitioned, cooperative) for drop-in parity.
+//
+// Declared grouping of the grouped fold (tiler_cuda_grouping, oracle
+// oracle_grid_fold restates the same order):
+//   level 1  exact contiguous partitions, one CTA each
+//            (strict_partial_sums, crates/tiler-reference/src/evaluate.rs:612-832);
+//   level 2  the ADR-0100 composition inside the CTA: block (r, g, l) owns the
+//            k contributors at (r*T + g*32 + l)*k, folded strictly; an
+//            ascending-mask XOR butterfly over the 32 lanes (result lane 0);
+//            a strict fold over the G warp slots; round totals in ascending
+//            order, round 0 peeled (docs/decisions/0100-...md decisions 1-5);
+//            tail padding with the two-sided identity (-0.0 / -inf);
+//   level 3  the last CTA of a row folds the partials: strictly (the second
+//            pass of strict_partitioned_sum) or by a second composition.
+// The data path reads each contributor once with 16-byte loads, all rounds'
+// loads issued before the folds consume them.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tc {
+
+template <int OP>
+__device__ __forceinline__ float fold2(float a, float b) {
+  if (OP == 0) return __fadd_rn(a, b);
+  return maximum(a, b);
+}
+
+template <int OP>
+__device__ __forceinline__ float identity_value() {
+  return OP == 0 ? __uint_as_float(0x80000000u) : __uint_as_float(0xff800000u);
+}
+
+// Ascending-mask butterfly (docs/decisions/0094-...md decision 4).
+template <int OP>
+__device__ __forceinline__ float butterfly(float v) {
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) v = fold2<OP>(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+
+// Folds one sequence seq[0, n) under the composition (T = blockDim.x, k, R)
+// and returns the result in thread 0 (unCanonicalized).  `slots` is
+// shared scratch of R*G floats plus R floats.  All threads must call it.
+template <int OP, int K>
+__device__ float compose_block(const float* __restrict__ seq, uint64_t n, uint32_t R, float* slots,
+                               bool vec_ok) {
+  const uint32_t T = blockDim.x, G = T >> 5, tid = threadIdx.x;
+  const uint32_t warp = tid >> 5, lane = tid & 31;
+  const float ident = identity_value<OP>();
+  constexpr uint32_t CH = 8;  // rounds whose loads are in flight together
+  for (uint32_t r0 = 0; r0 < R; r0 += CH) {
+    float vals[CH][K];
+#pragma unroll
+    for (uint32_t c = 0; c < CH; ++c) {
+      uint64_t base = ((uint64_t)(r0 + c) * T + tid) * K;
+      if constexpr (K == 4) {
+        if (r0 + c < R && base + K <= n && vec_ok) {
+          float4 v = __ldcs(reinterpret_cast<const float4*>(seq + base));
+          vals[c][0] = v.x; vals[c][1] = v.y; vals[c][2] = v.z; vals[c][3] = v.w;
+          continue;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < K; ++i) vals[c][i] = (r0 + c < R && base + i < n) ? __ldcs(seq + base + i) : ident;
+    }
+#pragma unroll
+    for (uint32_t c = 0; c < CH; ++c) {
+      if (r0 + c >= R) break;
+      float v = vals[c][0];
+#pragma unroll
+      for (int i = 1; i < K; ++i) v = fold2<OP>(v, vals[c][i]);
+      v = butterfly<OP>(v);
+      if (lane == 0) slots[(r0 + c) * G + warp] = v;
+    }
+  }
+  __syncthreads();
+  float* staged = slots + R * G;
+  for (uint32_t r = tid; r < R; r += T) {
+    float s = slots[r * G];
+    for (uint32_t g = 1; g < G; ++g) s = fold2<OP>(s, slots[r * G + g]);
+    staged[r] = s;
+  }
+  __syncthreads();
+  float total = 0.0f;
+  if (tid == 0) {
+    total = staged[0];
+    for (uint32_t r = 1; r < R; ++r) total = fold2<OP>(total, staged[r]);
+  }
+  __syncthreads();  // slots may be reused by the caller
+  return total;
+}
+
+// Runtime-k variant for the level-3 combine and small partitions.
+template <int OP>
+__device__ float compose_block_generic(const float* seq, uint64_t n, uint32_t T, uint32_t k, uint32_t R,
+                                       float* slots, bool use_cg) {
+  const uint32_t G = T >> 5, tid = threadIdx.x;
+  const uint32_t warp = tid >> 5, lane = tid & 31;
+  const float ident = identity_value<OP>();
+  if (tid < T) {
+    for (uint32_t r = 0; r < R; ++r) {
+      uint64_t base = ((uint64_t)r * T + tid) * k;
+      float v = ident;
+      for (uint32_t i = 0; i < k; ++i) {
+        float c = base + i < n ? (use_cg ? __ldcg(seq + base + i) : seq[base + i]) : ident;
+        v = i == 0 ? c : fold2<OP>(v, c);
+      }
+      v = butterfly<OP>(v);
+      if (lane == 0) slots[r * G + warp] = v;
+    }
+  }
+  __syncthreads();
+  float* staged = slots + R * G;
+  for (uint32_t r = tid; r < R; r += blockDim.x) {
+    float s = slots[r * G];
+    for (uint32_t g = 1; g < G; ++g) s = fold2<OP>(s, slots[r * G + g]);
+    staged[r] = s;
+  }
+  __syncthreads();
+  float total = 0.0f;
+  if (tid == 0) {
+    total = staged[0];
+    for (uint32_t r = 1; r < R; ++r) total = fold2<OP>(total, staged[r]);
+  }
+  __syncthreads();
+  return total;
+}
+
+template <int OP, int K>
+__global__ void __launch_bounds__(1024) grouped_fold_kernel(const float* __restrict__ x, uint64_t count,
+                                                            GroupedParams gp, float* __restrict__ partials,
+                                                            unsigned int* __restrict__ tickets,
+                                                            float* __restrict__ out) {
+  extern __shared__ float slots[];
+  const uint64_t P = gp.partitions;
+  const uint64_t row = blockIdx.x / P, p = blockIdx.x % P;
+  const uint64_t per = count / P;
+  const float* seq = x + row * count + p * per;
+  const bool vec_ok = ((reinterpret_cast<uintptr_t>(seq) & 15u) == 0);
+  float partial = compose_block<OP, K>(seq, per, gp.rounds, slots, vec_ok);
+  if (P == 1) {
+    if (threadIdx.x == 0) out[row] = canon(partial);
+    return;
+  }
+  __shared__ unsigned int is_last;
+  if (threadIdx.x == 0) {
+    partials[row * P + p] = partial;
+    __threadfence();
+    unsigned int ticket = atomicAdd(&tickets[row], 1u);
+    is_last = (ticket == P - 1);
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const float* pr = partials + row * P;
+  float total;
+  if (gp.combine_threads == 0) {
+    total = 0.0f;
+    if (threadIdx.x == 0) {
+      total = __ldcg(pr);
+      for (uint64_t i = 1; i < P; ++i) total = fold2<OP>(total, __ldcg(pr + i));
+    }
+  } else {
+    total = compose_block_generic<OP>(pr, P, gp.combine_threads, gp.combine_k, gp.combine_rounds, slots, true);
+  }
+  if (threadIdx.x == 0) {
+    out[row] = canon(total);
+    tickets[row] = 0;  // leaves the workspace ready for the next launch
+  }
+}
+
+void launch_grouped_fold(int op, const float* x, uint64_t rows, uint64_t count, const GroupedParams& gp,
+                         float* partials, unsigned int* tickets, float* out, cudaStream_t stream) {
+  const uint32_t G = gp.threads / 32;
+  uint32_t R = gp.rounds;
+  uint32_t cR = gp.combine_threads ? gp.combine_rounds : 0;
+  uint32_t cG = gp.combine_threads / 32;
+  size_t smem = sizeof(float) * (size_t)std::max<uint64_t>((uint64_t)R * G + R, (uint64_t)cR * cG + cR);
+  dim3 grid((unsigned)(rows * gp.partitions));
+  if (op == 0) {
+    if (gp.k == 4)
+      grouped_fold_kernel<0, 4><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
+    else if (gp.k == 2)
+      grouped_fold_kernel<0, 2><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
+    else
+      grouped_fold_kernel<0, 1><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
+  } else {
+    if (gp.k == 4)
+      grouped_fold_kernel<1, 4><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
+    else if (gp.k == 2)
+      grouped_fold_kernel<1, 2><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
+    else
+      grouped_fold_kernel<1, 1><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
+  }
+}
+
+// ---- reference-vocabulary groupings ------------------------------------------
+
+// strict_sum (evaluate.rs:498-589): one thread folds one row in order.
+__global__ void strict_sum_kernel(const float* __restrict__ x, uint64_t rows, uint64_t count,
+                                  float* __restrict__ out) {
+  uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  if (count == 0) { out[r] = 0.0f; return; }
+  const float* s = x + r * count;
+  float acc = s[0];
+  for (uint64_t i = 1; i < count; ++i) acc = __fadd_rn(acc, s[i]);
+  out[r] = canon(acc);
+}
+
+void launch_strict_sum(const float* x, uint64_t rows, uint64_t count, float* out, cudaStream_t stream) {
+  unsigned threads = 128;
+  strict_sum_kernel<<<(unsigned)((rows + threads - 1) / threads), threads, 0, stream>>>(x, rows, count, out);
+}
+
+// strict_partial_sums (evaluate.rs:612-747): one thread per partition.
+__global__ void partial_sums_kernel(const float* __restrict__ x, uint64_t rows, uint64_t count, uint64_t P,
+                                    uint64_t per, float* __restrict__ partials) {
+  uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i >= rows * P) return;
+  uint64_t r = i / P, p = i % P;
+  if (per == 0) { partials[i] = 0.0f; return; }
+  const float* s = x + r * count + p * per;
+  float acc = s[0];
+  for (uint64_t j = 1; j < per; ++j) acc = __fadd_rn(acc, s[j]);
+  partials[i] = canon(acc);
+}
+
+void launch_partitioned_sum(const float* x, uint64_t rows, uint64_t count, uint64_t P, uint64_t per,
+                            float* partials, float* out, cudaStream_t stream) {
+  unsigned threads = 128;
+  partial_sums_kernel<<<(unsigned)((rows * P + threads - 1) / threads), threads, 0, stream>>>(x, rows, count, P,
+                                                                                            per, partials);
+  launch_strict_sum(partials, rows, P, out, stream);
+}
+
+// cooperative_grouped_sum / fold_cooperative_sequence (evaluate.rs:936-1158):
+// one CTA per row; each round the participants' strict partials are staged in
+// shared memory and folded in ascending participant order by one thread.
+__global__ void cooperative_sum_kernel(const float* __restrict__ x, uint64_t count, uint64_t participants,
+                                       uint64_t per, uint64_t rounds, int participant_major,
+                                       float* __restrict__ out) {
+  extern __shared__ float staged[];
+  const float* s = x + blockIdx.x * count;
+  float total = 0.0f;
+  for (uint64_t r = 0; r < rounds; ++r) {
+    for (uint64_t p = threadIdx.x; p < participants; p += blockDim.x) {
+      uint64_t cell = participant_major ? p * rounds + r : r * participants + p;
+      const float* c = s + cell * per;
+      float partial = c[0];
+      for (uint64_t i = 1; i < per; ++i) partial = __fadd_rn(partial, c[i]);
+      staged[p] = partial;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float st = staged[0];
+      for (uint64_t p = 1; p < participants; ++p) st = __fadd_rn(st, staged[p]);
+      total = r == 0 ? st : __fadd_rn(total, st);
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[blockIdx.x] = canon(total);
+}
+
+void launch_cooperative_sum(const float* x, uint64_t rows, uint64_t count, uint64_t participants, uint64_t per,
+                            uint64_t rounds, int participant_major, float* out, cudaStream_t stream) {
+  unsigned threads = (unsigned)std::min<uint64_t>(participants, 1024);
+  threads = std::max(32u, (threads + 31) / 32 * 32);
+  size_t smem = participants * sizeof(float);
+  cooperative_sum_kernel<<<(unsigned)rows, threads, smem, stream>>>(x, count, participants, per, rounds,
+                                                                   participant_major, out);
+}
+
+}  // namespace tc

@@ -1,0 +1,572 @@
+// Row families: RMS normalization (f32 / bf16), max-shifted softmax with the
+// causal block mask, and the per-row int8 strict-affine quantize / decode.
+//
+// Each row family's reference fold is a strict left fold along the row
+// (rms_norm.rs:147-170 sum of squares, softmax.rs:295-300 denominator), a
+// dependent chain of adds that no reassociation may shorten.  The kernels
+// therefore give every row its own lane for the chain and keep the other
+// warps busy moving bytes: the chain reads staged copies from shared memory
+// while HBM traffic stays one read (plus an L2-resident re-read for RMS) and
+// one write per element.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tc {
+
+// ---------------------------------------------------------------------------
+// RMS normalization
+// ---------------------------------------------------------------------------
+//
+// Per CTA: a contiguous block of rows, processed in groups of up to GR (<= 32)
+// rows.  Warp 0 (one elected lane) streams 256-byte row chunks of the group
+// into a ring of shared-memory stages with cp.async.bulk (one mbarrier per
+// stage, loads marked L2 evict_last); warp 1 is the chain warp, lane r folding
+// row r's squares strictly from the staged chunks; once a group's scales are
+// known (mean = total/N, t = mean + eps, correctly rounded 1/sqrt(t)) the
+// normalize warps re-read the group's rows (an L2 hit: the rows were loaded a
+// few microseconds earlier; read with evict_first) and write y = w*(x*s) with
+// streaming stores, while the producer and the chain warp already work on
+// the next group.
+
+constexpr int kRmsChunkBytes = 256;
+constexpr int kRmsPitch = kRmsChunkBytes + 16;  // conflict-free float4 reads down a column of rows
+constexpr int kRmsStages = 8;
+constexpr int kRmsMaxGroup = 32;
+constexpr int kRmsNormWarps = 6;
+constexpr int kRmsThreads = 32 * (2 + kRmsNormWarps);
+
+struct RmsSmem {
+  alignas(128) uint8_t stage[kRmsStages][kRmsMaxGroup][kRmsPitch];
+  uint64_t full[kRmsStages];
+  uint64_t empty[kRmsStages];
+  uint64_t scale_full[2];
+  uint64_t scale_empty[2];
+  float scale[2][kRmsMaxGroup];
+  int abort;
+};
+
+template <bool BF16>
+struct RmsElem;
+template <>
+struct RmsElem<false> {
+  using T = float;
+  static constexpr int kPerVec = 4;
+  __device__ static void unpack(const uint4& v, float* o) {
+    o[0] = __uint_as_float(v.x); o[1] = __uint_as_float(v.y); o[2] = __uint_as_float(v.z); o[3] = __uint_as_float(v.w);
+  }
+  __device__ static uint4 pack(const float* o) {
+    return make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3]));
+  }
+};
+template <>
+struct RmsElem<true> {
+  using T = uint16_t;
+  static constexpr int kPerVec = 8;
+  __device__ static void unpack(const uint4& v, float* o) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[2 * i] = __uint_as_float(w[i] << 16);
+      o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ static uint4 pack(const float* o) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = (uint32_t)f32_to_bf16(o[2 * i]) | ((uint32_t)f32_to_bf16(o[2 * i + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+__device__ __forceinline__ uint4 ld_u4_policy(const void* p, uint64_t policy) {
+  uint4 v;
+  asm volatile("ld.global.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(policy));
+  return v;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kRmsThreads) rms_norm_kernel(const uint8_t* __restrict__ x,
+                                                              const uint8_t* __restrict__ w, int64_t w_row_stride,
+                                                              uint64_t rows, uint64_t extent, float eps,
+                                                              uint8_t* __restrict__ y, uint32_t group_rows,
+                                                              tiler_cuda_status* st) {
+  using E = RmsElem<BF16>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  RmsSmem& S = *reinterpret_cast<RmsSmem*>(smem_raw);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint64_t esize = sizeof(typename E::T);
+  const uint64_t row_bytes = extent * esize;
+  const uint64_t rb = blockIdx.x * rows / gridDim.x, re = (blockIdx.x + 1) * rows / gridDim.x;
+  const uint64_t my_rows = re - rb;
+  const uint32_t GR = group_rows;
+  const uint64_t ngroups = (my_rows + GR - 1) / GR;
+  const uint64_t nchunks = (row_bytes + kRmsChunkBytes - 1) / kRmsChunkBytes;
+  const uint64_t total = ngroups * nchunks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRmsStages; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&S.scale_full[s], 1); mbar_init(&S.scale_empty[s], kRmsNormWarps); }
+    S.abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (ngroups == 0) return;
+
+  if (warp == 0) {
+    // ---- producer: one lane issues every bulk copy --------------------------
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      for (uint64_t i = 0; i < total; ++i) {
+        const uint32_t stage = i % kRmsStages;
+        const uint64_t use = i / kRmsStages;
+        if (use > 0 && !mbar_wait(&S.empty[stage], (uint32_t)((use - 1) & 1), st)) { S.abort = 1; break; }
+        if (*(volatile int*)&S.abort) break;
+        const uint64_t g = i / nchunks, c = i % nchunks;
+        const uint32_t gr = (uint32_t)umin64(GR, my_rows - g * GR);
+        const uint32_t bytes = (uint32_t)umin64(kRmsChunkBytes, row_bytes - c * kRmsChunkBytes);
+        mbar_arrive_expect_tx(&S.full[stage], gr * bytes);
+        for (uint32_t r = 0; r < gr; ++r) {
+          const uint8_t* src = x + (rb + g * GR + r) * row_bytes + c * kRmsChunkBytes;
+          bulk_g2s(&S.stage[stage][r][0], src, bytes, &S.full[stage], keep);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- chain warp: lane r folds row r's squares in order -------------------
+    for (uint64_t g = 0; g < ngroups; ++g) {
+      const uint32_t gr = (uint32_t)umin64(GR, my_rows - g * GR);
+      float acc = 0.0f;
+      bool first = true;
+      for (uint64_t c = 0; c < nchunks; ++c) {
+        const uint64_t i = g * nchunks + c;
+        const uint32_t stage = i % kRmsStages;
+        if (!mbar_wait(&S.full[stage], (uint32_t)((i / kRmsStages) & 1), st)) S.abort = 1;
+        if (*(volatile int*)&S.abort) return;
+        const uint32_t bytes = (uint32_t)umin64(kRmsChunkBytes, row_bytes - c * kRmsChunkBytes);
+        if (lane < gr) {
+          const uint4* src = reinterpret_cast<const uint4*>(&S.stage[stage][lane][0]);
+          const uint32_t nvec = bytes / 16;
+#pragma unroll 4
+          for (uint32_t v = 0; v < nvec; ++v) {
+            float e[E::kPerVec];
+            E::unpack(src[v], e);
+#pragma unroll
+            for (int j = 0; j < E::kPerVec; ++j) {
+              const float sq = __fmul_rn(e[j], e[j]);
+              acc = first ? sq : __fadd_rn(acc, sq);
+              first = false;
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[stage]);
+      }
+      // rms_norm.rs:172-193: mean = total / N, t = mean + eps, certified rsqrt
+      const float mean = __fdiv_rn(acc, (float)extent);
+      const float s = rsqrt_cr(__fadd_rn(mean, eps));
+      const uint32_t slot = g & 1;
+      const uint64_t use = g >> 1;
+      if (use > 0 && !mbar_wait(&S.scale_empty[slot], (uint32_t)((use - 1) & 1), st)) S.abort = 1;
+      if (*(volatile int*)&S.abort) return;
+      if (lane < gr) S.scale[slot][lane] = s;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.scale_full[slot]);
+    }
+  } else {
+    // ---- normalize warps: y = w * (x * s), two roundings (rms_norm.rs:479-485)
+    const uint32_t nw = warp - 2;
+    const uint64_t drop = policy_evict_first();
+    const uint64_t nvec = row_bytes / 16;
+    for (uint64_t g = 0; g < ngroups; ++g) {
+      const uint32_t gr = (uint32_t)umin64(GR, my_rows - g * GR);
+      const uint32_t slot = g & 1;
+      if (!mbar_wait(&S.scale_full[slot], (uint32_t)((g >> 1) & 1), st)) S.abort = 1;
+      if (*(volatile int*)&S.abort) return;
+      for (uint32_t r = nw; r < gr; r += kRmsNormWarps) {
+        const float s = S.scale[slot][r];
+        const uint64_t row = rb + g * GR + r;
+        const uint8_t* xr = x + row * row_bytes;
+        const uint8_t* wr = w + (int64_t)row * w_row_stride * (int64_t)esize;
+        uint8_t* yr = y + row * row_bytes;
+        for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * 4) {
+          uint4 xv[4], wv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint64_t v = v0 + 32 * u;
+            if (v < nvec) {
+              xv[u] = ld_u4_policy(xr + v * 16, drop);
+              wv[u] = __ldg(reinterpret_cast<const uint4*>(wr + v * 16));
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint64_t v = v0 + 32 * u;
+            if (v < nvec) {
+              float xe[E::kPerVec], we[E::kPerVec], ye[E::kPerVec];
+              E::unpack(xv[u], xe);
+              E::unpack(wv[u], we);
+#pragma unroll
+              for (int j = 0; j < E::kPerVec; ++j) ye[j] = canon(__fmul_rn(we[j], __fmul_rn(xe[j], s)));
+              st_global_stream_u4(reinterpret_cast<uint4*>(yr + v * 16), E::pack(ye));
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.scale_empty[slot]);
+    }
+  }
+}
+
+// Any-shape path (unaligned rows or extents not a multiple of 16 bytes): one
+// warp per row, lane 0 folds the squares straight from global memory.
+template <bool BF16>
+__global__ void rms_norm_generic_kernel(const void* __restrict__ xv, const void* __restrict__ wv,
+                                        int64_t w_row_stride, uint64_t rows, uint64_t extent, float eps,
+                                        void* __restrict__ yv) {
+  using T = typename RmsElem<BF16>::T;
+  const T* x = (const T*)xv;
+  const T* w = (const T*)wv;
+  T* y = (T*)yv;
+  const uint64_t row = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  const uint32_t lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  auto ld = [](const T* p, uint64_t i) -> float {
+    if constexpr (BF16) return bf16_to_f32(p[i]); else return p[i];
+  };
+  float s = 0.0f;
+  if (lane == 0) {
+    float acc = 0.0f;
+    for (uint64_t i = 0; i < extent; ++i) {
+      const float v = ld(x + row * extent, i);
+      const float sq = __fmul_rn(v, v);
+      acc = i == 0 ? sq : __fadd_rn(acc, sq);
+    }
+    s = rsqrt_cr(__fadd_rn(__fdiv_rn(acc, (float)extent), eps));
+  }
+  s = __shfl_sync(0xffffffffu, s, 0);
+  for (uint64_t i = lane; i < extent; i += 32) {
+    const float v = canon(__fmul_rn(ld(w + (int64_t)row * w_row_stride, i), __fmul_rn(ld(x + row * extent, i), s)));
+    if constexpr (BF16) y[row * extent + i] = f32_to_bf16(v); else y[row * extent + i] = v;
+  }
+}
+
+int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,
+                    float eps, void* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  if (rows == 0 || extent == 0) return 0;
+  const uint64_t esize = bf16 ? 2 : 4;
+  const bool aligned = ((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0) && ((uintptr_t)w % 16 == 0) &&
+                       ((extent * esize) % 16 == 0);
+  if (!aligned) {
+    const unsigned wpb = 8;
+    const unsigned blocks = (unsigned)((rows + wpb - 1) / wpb);
+    if (bf16)
+      rms_norm_generic_kernel<true><<<blocks, wpb * 32, 0, stream>>>(x, w, w_row_stride, rows, extent, eps, y);
+    else
+      rms_norm_generic_kernel<false><<<blocks, wpb * 32, 0, stream>>>(x, w, w_row_stride, rows, extent, eps, y);
+    return 0;
+  }
+  // One CTA per SM; each takes rows/grid consecutive rows in groups of GR.
+  const uint64_t grid = umin64((uint64_t)sm_count, rows);
+  const uint64_t per_cta = (rows + grid - 1) / grid;
+  uint32_t gr = 16;
+  if (per_cta < gr) gr = (uint32_t)per_cta;
+  const size_t smem = sizeof(RmsSmem);
+  if (bf16) {
+    cudaFuncSetAttribute(rms_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    rms_norm_kernel<true><<<(unsigned)grid, kRmsThreads, smem, stream>>>(
+        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, gr, st);
+  } else {
+    cudaFuncSetAttribute(rms_norm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    rms_norm_kernel<false><<<(unsigned)grid, kRmsThreads, smem, stream>>>(
+        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, gr, st);
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Softmax (softmax.rs:260-315) with the in-kernel causal block mask.
+// ---------------------------------------------------------------------------
+//
+// One warp per row at a time, the row staged once in shared memory by a bulk
+// copy.  The maximum (order-free) is a lane-parallel fold plus butterfly; the
+// exponentials are written back over the staged row; lane 0 folds the
+// denominator strictly from shared memory; r = 1/d; out = e * r with
+// streaming stores.  Three CTAs of eight warps per SM keep 24 chains in
+// flight per SM.
+
+constexpr int kSmxWarps = 8;  // at most; fewer for long rows (shared memory)
+constexpr uint64_t kSmxMaxExtent = 8192;
+
+__device__ __forceinline__ float masked_value(float v, uint64_t col, uint64_t diag, bool causal) {
+  return (causal && col > diag) ? __fadd_rn(v, __uint_as_float(0xff800000u)) : v;
+}
+
+__global__ void __launch_bounds__(kSmxWarps * 32) softmax_staged_kernel(const float* __restrict__ x, uint64_t rows,
+                                                                     uint64_t extent, uint64_t period,
+                                                                     uint64_t row_offset, float* __restrict__ y,
+                                                                     tiler_cuda_status* st) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  double* table = reinterpret_cast<double*>(smem_raw);  // 256 doubles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + 2048);
+  float* bufs = reinterpret_cast<float*>(smem_raw + 2048 + 128);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t wpb = blockDim.x >> 5;
+  load_exp_table(table);
+  if (threadIdx.x < wpb) mbar_init(&bars[threadIdx.x], 1);
+  fence_barrier_init();
+  __syncthreads();
+  float* buf = bufs + warp * extent;
+  float4* buf4 = reinterpret_cast<float4*>(buf);
+  const uint64_t nvec = extent / 4;
+  const bool causal = period != 0;
+  const uint64_t drop = policy_evict_first();
+  uint32_t iter = 0;
+  for (uint64_t row = (uint64_t)blockIdx.x * wpb + warp; row < rows; row += (uint64_t)gridDim.x * wpb, ++iter) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bars[warp], (uint32_t)(extent * 4));
+      bulk_g2s(buf, x + row * extent, (uint32_t)(extent * 4), &bars[warp], drop);
+    }
+    if (!mbar_wait(&bars[warp], iter & 1, st)) return;
+    const uint64_t diag = causal ? (row_offset + row) % period : 0;
+    // maximum fold (order-free: any grouping is bit-exact, softmax/tests.rs:118)
+    float m = __uint_as_float(0xff800000u);
+    for (uint64_t v = lane; v < nvec; v += 32) {
+      const float4 q = buf4[v];
+      const uint64_t c = v * 4;
+      m = maximum(m, masked_value(q.x, c, diag, causal));
+      m = maximum(m, masked_value(q.y, c + 1, diag, causal));
+      m = maximum(m, masked_value(q.z, c + 2, diag, causal));
+      m = maximum(m, masked_value(q.w, c + 3, diag, causal));
+    }
+#pragma unroll
+    for (int k = 1; k < 32; k <<= 1) m = maximum(m, __shfl_xor_sync(0xffffffffu, m, k));
+    // e_i = exp(x_i - m), one subtraction rounding then the certified exp
+    for (uint64_t v = lane; v < nvec; v += 32) {
+      float4 q = buf4[v];
+      const uint64_t c = v * 4;
+      q.x = exp_cr(__fsub_rn(masked_value(q.x, c, diag, causal), m), table, st);
+      q.y = exp_cr(__fsub_rn(masked_value(q.y, c + 1, diag, causal), m), table, st);
+      q.z = exp_cr(__fsub_rn(masked_value(q.z, c + 2, diag, causal), m), table, st);
+      q.w = exp_cr(__fsub_rn(masked_value(q.w, c + 3, diag, causal), m), table, st);
+      buf4[v] = q;
+    }
+    __syncwarp();
+    float rcp = 0.0f;
+    if (lane == 0) {
+      float d = buf[0];
+      float4 q = buf4[0];
+      d = __fadd_rn(__fadd_rn(__fadd_rn(d, q.y), q.z), q.w);
+#pragma unroll 8
+      for (uint64_t v = 1; v < nvec; ++v) {
+        q = buf4[v];
+        d = __fadd_rn(d, q.x);
+        d = __fadd_rn(d, q.y);
+        d = __fadd_rn(d, q.z);
+        d = __fadd_rn(d, q.w);
+      }
+      rcp = __fdiv_rn(1.0f, d);
+    }
+    rcp = __shfl_sync(0xffffffffu, rcp, 0);
+    float4* yr = reinterpret_cast<float4*>(y + row * extent);
+    for (uint64_t v = lane; v < nvec; v += 32) {
+      float4 q = buf4[v];
+      q.x = canon(__fmul_rn(q.x, rcp));
+      q.y = canon(__fmul_rn(q.y, rcp));
+      q.z = canon(__fmul_rn(q.z, rcp));
+      q.w = canon(__fmul_rn(q.w, rcp));
+      st_global_stream(yr + v, q);
+    }
+    __syncwarp();  // the buffer is reloaded next iteration
+  }
+}
+
+// Any-shape path: one warp per row, y doubles as the exponential scratch.
+__global__ void softmax_generic_kernel(const float* __restrict__ x, uint64_t rows, uint64_t extent, uint64_t period,
+                                       uint64_t row_offset, float* __restrict__ y, tiler_cuda_status* st) {
+  __shared__ double table[256];
+  load_exp_table(table);
+  __syncthreads();
+  const uint64_t row = blockIdx.x * (uint64_t)(blockDim.x / 32) + threadIdx.x / 32;
+  const uint32_t lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + row * extent;
+  float* yr = y + row * extent;
+  const bool causal = period != 0;
+  const uint64_t diag = causal ? (row_offset + row) % period : 0;
+  float m = __uint_as_float(0xff800000u);
+  for (uint64_t i = lane; i < extent; i += 32) m = maximum(m, masked_value(xr[i], i, diag, causal));
+#pragma unroll
+  for (int k = 1; k < 32; k <<= 1) m = maximum(m, __shfl_xor_sync(0xffffffffu, m, k));
+  for (uint64_t i = lane; i < extent; i += 32) yr[i] = exp_cr(__fsub_rn(masked_value(xr[i], i, diag, causal), m), table, st);
+  __syncwarp();
+  float rcp = 0.0f;
+  if (lane == 0) {
+    float d = yr[0];
+    for (uint64_t i = 1; i < extent; ++i) d = __fadd_rn(d, yr[i]);
+    rcp = __fdiv_rn(1.0f, d);
+  }
+  rcp = __shfl_sync(0xffffffffu, rcp, 0);
+  __syncwarp();
+  for (uint64_t i = lane; i < extent; i += 32) yr[i] = canon(__fmul_rn(yr[i], rcp));
+}
+
+int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t causal_period, uint64_t row_offset,
+                   float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  if (rows == 0 || extent == 0) return 0;
+  const bool staged = (extent % 4 == 0) && extent <= kSmxMaxExtent && ((uintptr_t)x % 16 == 0) &&
+                      ((uintptr_t)y % 16 == 0);
+  if (!staged) {
+    const unsigned wpb = 8;
+    softmax_generic_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, stream>>>(x, rows, extent,
+                                                                                       causal_period, row_offset, y, st);
+    return 0;
+  }
+  const size_t smem = 2048 + 128 + (size_t)kSmxWarps * extent * 4;
+  cudaFuncSetAttribute(softmax_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int per_sm = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, softmax_staged_kernel, kSmxWarps * 32, smem);
+  per_sm = std::max(per_sm, 1);
+  const uint64_t want = (rows + kSmxWarps - 1) / kSmxWarps;
+  const unsigned grid = (unsigned)umin64(want, (uint64_t)sm_count * per_sm);
+  softmax_staged_kernel<<<grid, kSmxWarps * 32, smem, stream>>>(x, rows, extent, causal_period, row_offset, y, st);
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Per-row int8 strict-affine quantize and decode.
+// ---------------------------------------------------------------------------
+//
+// One CTA per row.  Pass 1 folds max|x| (order-free maximum) and finds the
+// first NaN; scale = max/127 (one division), refused unless positive-normal;
+// pass 2 (an L1/L2-resident re-read) forms code = RNE(clamp(x/scale)).  The
+// quotient is formed as x * (1/scale) and taken only when it is provably on
+// the same side of every half-integer as the correctly rounded x/scale
+// (|error| < 2^-16 below 128); within 2.5e-5 of a half-integer the exact
+// IEEE division decides, so codes equal the oracle's bit for bit.
+
+constexpr int kQThreads = 256;
+
+__device__ __forceinline__ int8_t code_of(float xv, float scale, float inv) {
+  float q = __fmul_rn(xv, inv);
+  const float frac = fabsf(q - truncf(q));
+  if (fabsf(frac - 0.5f) < 2.5e-5f || !isfinite(q)) q = __fdiv_rn(xv, scale);
+  q = __fadd_rn(q, 0.0f);
+  q = fminf(fmaxf(q, -127.0f), 127.0f);
+  return (int8_t)__float2int_rn(q);
+}
+
+__global__ void __launch_bounds__(kQThreads) quantize_i8_rows_kernel(const float* __restrict__ x, uint64_t extent,
+                                                                    int8_t* __restrict__ codes,
+                                                                    float* __restrict__ scales,
+                                                                    tiler_cuda_status* st) {
+  __shared__ float red[kQThreads / 32];
+  __shared__ unsigned long long nan_at[kQThreads / 32];
+  const uint64_t row = blockIdx.x;
+  const float* xr = x + row * extent;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool vec = (extent % 4 == 0) && ((uintptr_t)x % 16 == 0);
+  float m = 0.0f;
+  unsigned long long first_nan = ~0ull;
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    for (uint64_t v = threadIdx.x; v < extent / 4; v += kQThreads) {
+      const float4 q = __ldg(x4 + v);
+      const float e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (isnan(e[j]) && first_nan == ~0ull) first_nan = v * 4 + j;
+        m = maximum(m, fabsf(e[j]));
+      }
+    }
+  } else {
+    for (uint64_t i = threadIdx.x; i < extent; i += kQThreads) {
+      const float e = xr[i];
+      if (isnan(e) && first_nan == ~0ull) first_nan = i;
+      m = maximum(m, fabsf(e));
+    }
+  }
+#pragma unroll
+  for (int k = 1; k < 32; k <<= 1) {
+    m = maximum(m, __shfl_xor_sync(0xffffffffu, m, k));
+    first_nan = min(first_nan, (unsigned long long)__shfl_xor_sync(0xffffffffu, first_nan, k));
+  }
+  if (lane == 0) { red[warp] = m; nan_at[warp] = first_nan; }
+  __syncthreads();
+  m = red[0];
+  first_nan = nan_at[0];
+  for (int i = 1; i < kQThreads / 32; ++i) { m = maximum(m, red[i]); first_nan = min(first_nan, nan_at[i]); }
+  if (first_nan != ~0ull) {
+    if (threadIdx.x == 0) report_error(st, row * extent + first_nan, TILER_CUDA_NAN_INPUT);
+    return;
+  }
+  // maximum|x| over a NaN-free row; 0 stays +0 (all |x| are non-negative)
+  const float scale = __fdiv_rn(m, 127.0f);
+  if (threadIdx.x == 0) scales[row] = scale;
+  if (!(isnormal(scale) && scale > 0.0f)) {
+    if (threadIdx.x == 0) report_error(st, row * extent, TILER_CUDA_SCALE_DOMAIN);
+    return;
+  }
+  const float inv = __frcp_rn(scale);
+  int8_t* cr = codes + row * extent;
+  if (vec && ((uintptr_t)codes % 4 == 0)) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    char4* c4 = reinterpret_cast<char4*>(cr);
+    for (uint64_t v = threadIdx.x; v < extent / 4; v += kQThreads) {
+      const float4 q = __ldg(x4 + v);
+      c4[v] = make_char4(code_of(q.x, scale, inv), code_of(q.y, scale, inv), code_of(q.z, scale, inv),
+                         code_of(q.w, scale, inv));
+    }
+  } else {
+    for (uint64_t i = threadIdx.x; i < extent; i += kQThreads) cr[i] = code_of(xr[i], scale, inv);
+  }
+}
+
+void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
+                             tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  (void)sm_count;
+  if (rows == 0) return;
+  quantize_i8_rows_kernel<<<(unsigned)rows, kQThreads, 0, stream>>>(x, extent, codes, scales, st);
+}
+
+// dequantize_one with zero point 0 (quantization.rs:440-451).
+__global__ void dequantize_i8_rows_kernel(const int8_t* __restrict__ codes, const float* __restrict__ scales,
+                                          uint64_t rows, uint64_t extent, float* __restrict__ y) {
+  const uint64_t total = rows * extent;
+  const bool vec = (extent % 16 == 0) && ((uintptr_t)codes % 16 == 0) && ((uintptr_t)y % 16 == 0);
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const uint4* c16 = reinterpret_cast<const uint4*>(codes);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    for (uint64_t v = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; v < total / 16; v += stride) {
+      const uint4 c = ld_global_nc_u4(c16 + v);
+      const float s = __ldg(scales + (v * 16) / extent);
+      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int8_t code = (int8_t)((w[q] >> (8 * j)) & 0xff);
+          o[j] = code == 0 ? 0.0f : __fmul_rn((float)code, s);
+        }
+        st_global_stream(y4 + v * 4 + q, make_float4(o[0], o[1], o[2], o[3]));
+      }
+    }
+  } else {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
+      const int8_t code = codes[i];
+      y[i] = code == 0 ? 0.0f : __fmul_rn((float)code, scales[i / extent]);
+    }
+  }
+}
+
+void launch_dequantize_i8_rows(const int8_t* codes, const float* scales, uint64_t rows, uint64_t extent, float* y,
+                               int sm_count, cudaStream_t stream) {
+  if (rows == 0 || extent == 0) return;
+  dequantize_i8_rows_kernel<<<(unsigned)(sm_count * 8), 256, 0, stream>>>(codes, scales, rows, extent, y);
+}
+
+}  // namespace tc
