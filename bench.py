@@ -1,0 +1,411 @@
+"""Benchmark of the tiler-cuda hot path on B200 (the driver's contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tiler|reference]
+
+Headline workload (the metric's first config that
+fits one GPU): RMS normalization, x f32 [8192, 4096] ~ N(0,1), w f32 [4096]
+~ U[0.5, 1.5], eps = 1e-6 (bits 0x358637bd).  A step is one pass of the RMS
+kernel over one [8192, 4096] batch; steps rotate over enough input/output
+batches that the working set (>= 768 MB) is far larger than L2.
+
+`value` is algorithmic HBM bytes (read x + w, write y) over device time, in
+GB/s, summed over ranks (one process per GPU, each normalizing its own
+batches: weak scaling, no collective on the data path).  `e2e` measures the
+same metric through the public C-ABI entry point with the batch starting
+and ending in pinned host memory.  `families` carries the other BASELINE
+configs measured the same way (device time, CUDA events on the launching
+stream).  With --impl reference the CPU restatement of tiler-reference
+(oracle/, the only reference implementation runnable here) is timed on the
+host cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+EPS_BITS = 0x358637BD
+RMS_ROWS, RMS_EXTENT = 8192, 4096
+RMS_BYTES = RMS_ROWS * RMS_EXTENT * 4 * 2 + RMS_EXTENT * 4  # read x, read w, write y
+METRIC = "rms_norm_f32 HBM GB/s (per-family HBM GB/s; bf16 contraction TFLOP/s)"
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def committed_traffic(name):
+    """DRAM bytes per launch from the committed ncu summary profiles/<name>.txt
+    (line `traffic_bytes_per_launch: N`), else None."""
+    p = os.path.join(ROOT, "profiles", name + ".txt")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_device(fn, steps, warmup, world, clocks=None):
+    """Runs warmup untimed steps, then times exactly `steps` calls of fn(i)
+    with CUDA events on the current stream, barrier + synchronize on both
+    sides; returns (ms total, max over ranks)."""
+    import torch
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = clocks if clocks is not None else _Null()
+    with ctx:
+        e0.record(s)
+        for i in range(steps):
+            fn(i)
+        e1.record(s)
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    return max_over_ranks(e0.elapsed_time(e1), world)
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        pass
+
+
+def cpu_baseline_rms(nthreads, min_seconds=3.0):
+    """The oracle's RMS (tiler-reference semantics) on the host cores over a
+    bounded sample: the full [8192, 4096] batch, repeated until min_seconds."""
+    import numpy as np
+
+    import oracle
+    oracle.build()
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((RMS_ROWS, RMS_EXTENT), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, RMS_EXTENT).astype(np.float32)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.rms_norm_f32(x, w, EPS_BITS, nthreads=nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return RMS_BYTES * reps / el / 1e9, f"{reps} x full [8192,4096] batch, {el:.1f} s"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    import oracle
+    oracle.build()
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    sample_rows = 1024  # bounded sample: 1/8 of the batch per step
+    x = rng.standard_normal((sample_rows, RMS_EXTENT), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, RMS_EXTENT).astype(np.float32)
+    for _ in range(args.warmup):
+        oracle.rms_norm_f32(x, w, EPS_BITS, nthreads=cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.rms_norm_f32(x, w, EPS_BITS, nthreads=cores)
+    el = time.perf_counter() - t0
+    bytes_per_step = sample_rows * RMS_EXTENT * 8 + RMS_EXTENT * 4
+    v = bytes_per_step * args.steps / el / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) x, U[0.5,1.5] w)",
+            "config": {"workload": "rms_norm_f32 [8192,4096] eps=1e-6", "sample": f"{sample_rows} rows per step",
+                       "parallelism": f"{cores} host threads"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{sample_rows} of 8192 rows per step, {args.steps} steps"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "tiler-reference is Rust (nightly) and cannot be built here; its C++ restatement "
+                    "(oracle/, bit-identical results) is the reference arm"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def family_suite(fam, torch, world, steps_small, warmup):
+    """Per-family device throughput at the BASELINE configs (each config's own
+    algorithmic bytes / FLOPs; rotating buffers so inputs exceed L2)."""
+    hbm, tflops, _ = measured_peaks()
+    out = {}
+    gen = torch.Generator("cuda").manual_seed(7)
+    dev = "cuda"
+
+    def rec(name, unit, per_step, ms, steps, peak, launches=1):
+        v = per_step * steps / (ms / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+        out[name] = {"value": round(v, 2), "unit": unit, "frac": round(v / peak, 4),
+                     "us_per_launch": round(ms * 1e3 / steps / launches, 2)}
+
+    # two-level grouped sum, x f32 [2^24]
+    n = 1 << 24
+    xs = [torch.rand(n, device=dev, generator=gen) * 2 - 1 for _ in range(4)]
+    g = fam.plan_grouping(1, n)
+    ws = fam.grouped_workspace(1, g)
+    o = torch.empty(1, device=dev)
+    from tiler_b200 import _native as N
+    import ctypes as C
+    gs = N.Grouping.from_dict(g)
+    ctx, L = fam.context(), N.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def run_sum(i):
+        L.tiler_cuda_sum_f32(ctx, stream, xs[i % 4].data_ptr(), 1, n, C.byref(gs), ws.data_ptr(), ws.numel(),
+                             o.data_ptr())
+    ms = time_device(run_sum, steps_small * 4, warmup, world)
+    rec("sum_f32_2^24", "GB/s", n * 4, ms, steps_small * 4, hbm)
+    out["sum_f32_2^24"]["grouping"] = g
+    del xs
+
+    # RMS bf16 [8192, 4096]
+    xb = [torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=gen).to(torch.bfloat16) for _ in range(6)]
+    wb = (torch.rand(RMS_EXTENT, device=dev, generator=gen) + 0.5).to(torch.bfloat16)
+    yb = [torch.empty_like(xb[0]) for _ in range(2)]
+    ms = time_device(lambda i: fam.rms_norm(xb[i % 6], wb, out=yb[i % 2], check=False), steps_small * 4, warmup, world)
+    rec("rms_norm_bf16_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 4 + RMS_EXTENT * 2, ms, steps_small * 4, hbm)
+    del xb, yb
+
+    # softmax f32 [65536, 2048] with the causal block mask
+    xsm = torch.randn(65536, 2048, device=dev, generator=gen) * 3
+    ysm = torch.empty_like(xsm)
+    ms = time_device(lambda i: fam.softmax(xsm, causal_period=2048, out=ysm, check=False), steps_small, warmup, world)
+    rec("softmax_f32_65536x2048_causal", "GB/s", 65536 * 2048 * 8, ms, steps_small, hbm)
+    del xsm, ysm
+
+    # quantize / decode f32 [16384, 4096]
+    xq = [torch.randn(16384, 4096, device=dev, generator=gen) for _ in range(2)]
+    codes, scales = fam.quantize_i8_rows(xq[0])
+    ms = time_device(lambda i: fam.quantize_i8_rows(xq[i % 2], check=False), steps_small, warmup, world)
+    qbytes = 16384 * 4096 * 5 + 16384 * 4
+    rec("quantize_i8_16384x4096", "GB/s", qbytes, ms, steps_small, hbm)
+    yq = torch.empty(16384, 4096, device=dev)
+    cd = torch.empty_like(codes)
+
+    def run_dec(i):
+        L.tiler_cuda_dequantize_i8_rows(ctx, stream, codes.data_ptr(), scales.data_ptr(), 16384, 4096, yq.data_ptr())
+    ms = time_device(run_dec, steps_small, warmup, world)
+    rec("dequantize_i8_16384x4096", "GB/s", qbytes, ms, steps_small, hbm)
+    del xq, yq, codes, cd
+
+    # gather: ids i32 [8192] from bf16 table [128256, 4096]
+    table = (torch.randn(128256, 4096, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    idss = [torch.randint(0, 128256, (8192,), device=dev, dtype=torch.int32, generator=gen) for _ in range(8)]
+    ga = torch.empty(8192, 4096, device=dev, dtype=torch.bfloat16)
+    ms = time_device(lambda i: fam.gather_rows(table, idss[i % 8], out=ga, check=False), steps_small * 4, warmup,
+                     world)
+    rec("gather_bf16_8192_of_128256x4096", "GB/s", 8192 * 4 + 8192 * 4096 * 4, ms, steps_small * 4, hbm)
+
+    # bf16 contraction [8192,4096] x [4096,14336] + SiLU (W stored [N,K])
+    wt = (torch.randn(14336, 4096, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    cc = torch.empty(8192, 14336, device=dev, dtype=torch.bfloat16)
+    gsteps = max(2, steps_small // 2)
+    ms = time_device(lambda i: fam.gemm_bf16(ga, wt, "silu", out=cc, check=False), gsteps, warmup, world)
+    rec("gemm_bf16_silu_8192x4096x14336", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps, tflops)
+    del table, ga, wt, cc
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_tiler(args):
+    import torch
+
+    from tiler_b200 import families as fam
+    from tiler_b200 import _native as N
+    import ctypes as C
+
+    rank, world, local = dist_setup(args.gpus)
+    hbm, tflops, peak_kind = measured_peaks()
+    ctx, L = fam.context(), N.lib()
+    gen = torch.Generator("cuda").manual_seed(1234 + rank)
+    nbuf = 3
+    xs = [torch.randn(RMS_ROWS, RMS_EXTENT, device="cuda", generator=gen) for _ in range(nbuf)]
+    w = torch.rand(RMS_EXTENT, device="cuda", generator=gen) + 0.5
+    ys = [torch.empty_like(xs[0]) for _ in range(nbuf)]
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step(i):
+        L.tiler_cuda_rms_norm_f32(ctx, stream, None, xs[i % nbuf].data_ptr(), w.data_ptr(), 0, RMS_ROWS,
+                                  RMS_EXTENT, EPS_BITS, ys[i % nbuf].data_ptr())
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    ms = time_device(step, args.steps, args.warmup, world, clocks=clocks)
+    ms_step = ms / args.steps
+    value = RMS_BYTES * world * args.steps / (ms / 1e3) / 1e9
+    per_gpu = RMS_BYTES / (ms_step / 1e3) / 1e9
+    clk = clocks.summary() if clocks else None
+
+    # end to end through the public entry point: pinned host x -> device ->
+    # RMS -> pinned host y, every step
+    hx = torch.empty(RMS_ROWS, RMS_EXTENT, dtype=torch.float32, pin_memory=True)
+    hx.copy_(xs[0])
+    hy = torch.empty_like(hx, pin_memory=True)
+    dx, dy = xs[0], ys[0]
+
+    def e2e_step(i):
+        dx.copy_(hx, non_blocking=True)
+        L.tiler_cuda_rms_norm_f32(ctx, stream, None, dx.data_ptr(), w.data_ptr(), 0, RMS_ROWS, RMS_EXTENT,
+                                  EPS_BITS, dy.data_ptr())
+        hy.copy_(dy, non_blocking=True)
+    e2e_steps = max(3, min(args.steps, 20))
+    ms_e2e = time_device(e2e_step, e2e_steps, 2, world)
+    e2e_value = RMS_BYTES * world * e2e_steps / (ms_e2e / 1e3) / 1e9
+    del hx, hy
+
+    families = None
+    if not args.no_families:
+        del xs, ys
+        torch.cuda.empty_cache()
+        families = family_suite(fam, torch, world, args.family_steps, max(3, args.warmup))
+
+    if rank == 0:
+        cpu_v, cpu_sample = (None, None)
+        if world == 1 and not args.no_cpu_baseline:
+            cpu_v, cpu_sample = cpu_baseline_rms(os.cpu_count() or 1)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) x, U[0.5,1.5] w)",
+            "config": {"workload": "rms_norm_f32 [8192,4096] eps=1e-6 (BASELINE configs[1])",
+                       "l2": f"{nbuf} rotating input/output batches ({nbuf * 256} MB) > 126 MB L2",
+                       "parallelism": f"dp{world} (one [8192,4096] batch per GPU per step)"},
+            "gpu_launches": args.steps,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": RMS_ROWS * RMS_EXTENT * 4, "d2h_bytes_per_step": RMS_ROWS * RMS_EXTENT * 4,
+                    "steps": e2e_steps, "path": "tiler_cuda_rms_norm_f32 with pinned host buffers"},
+            "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": hbm, "unit": "GB/s",
+                         "frac": round(per_gpu / hbm, 4), "traffic": committed_traffic("rms_norm_f32_8192x4096"),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s",
+                         "algorithmic_bytes_per_launch": RMS_BYTES},
+            "clocks": clk,
+        }
+        if cpu_v is not None:
+            line["cpu_baseline"] = {"value": round(cpu_v, 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
+                                    "kind": "port", "sample": cpu_sample}
+        if families is not None:
+            line["families"] = families
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="tiler", choices=["tiler", "reference"])
+    ap.add_argument("--family-steps", type=int, default=20)
+    ap.add_argument("--no-families", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_tiler(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -173,7 +173,7 @@ def test_explicit_groupings_including_padding_and_strict_combine(fam, oracle_lib
     x = seeded_normal(9, 3 * 12_000).reshape(3, 12_000)
     for g in [dict(partitions=1, threads=64, k=1, rounds=188, combine_threads=0, combine_k=0, combine_rounds=0),
               dict(partitions=4, threads=128, k=4, rounds=6, combine_threads=0, combine_k=0, combine_rounds=0),
-              dict(partitions=100, threads=32, k=2, rounds=2, combine_threads=64, combine_k=1, combine_rounds=2),
+              dict(partitions=100, threads=64, k=2, rounds=1, combine_threads=64, combine_k=1, combine_rounds=2),
               dict(partitions=3, threads=1024, k=4, rounds=1, combine_threads=32, combine_k=1, combine_rounds=1)]:
         got = host(fam.sum_f32(cuda(x), g))
         st, want = oracle_lib.grid_fold(x, g, op=0)
