@@ -273,11 +273,13 @@ def test_scale_bias_matches_oracle(fam, oracle_lib):
     x = seeded_normal(1, 100_001)
     a = np.float32(1.0000001)
     b = np.float32(-3.5)
-    got = host(fam.scale_bias(cuda(x), cuda(np.array(a)), cuda(np.array(b))))
+    got = host(fam.scale_bias(cuda(x), torch.tensor(a).cuda(), torch.tensor(b).cuda()))
     _, want = oracle_lib.scale_bias_f32(x, a, b)
     assert_bits_equal(got, want)
     a2 = seeded_normal(2, 100_001)
-    got = host(fam.scale_bias(cuda(x), cuda(a2), cuda(np.array(b))))
+    got = host(fam.scale_bias(cuda(x), cuda(a2), torch.tensor(b).cuda()))
+    with pytest.raises(ValueError):
+        fam.scale_bias(cuda(x), cuda(a2[:10]), torch.tensor(b).cuda())
     _, want = oracle_lib.scale_bias_f32(x, a2, np.array([b]))
     assert_bits_equal(got, want)
 

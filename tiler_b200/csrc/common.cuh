@@ -22,6 +22,13 @@ constexpr uint32_t kCanonicalNan = 0x7fc00000u;
 
 __host__ __device__ __forceinline__ uint64_t umin64(uint64_t a, uint64_t b) { return a < b ? a : b; }
 
+__device__ __forceinline__ bool is_nan_bits(float v) { return (__float_as_uint(v) & 0x7fffffffu) > 0x7f800000u; }
+
+__device__ __forceinline__ bool is_positive_normal(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b >> 31) == 0 && (b >> 23) != 0 && (b >> 23) != 0xffu;
+}
+
 __device__ __forceinline__ float canon(float v) {
   return isnan(v) ? __uint_as_float(kCanonicalNan) : v;
 }

@@ -463,49 +463,54 @@ __global__ void __launch_bounds__(kQThreads) quantize_i8_rows_kernel(const float
                                                                     float* __restrict__ scales,
                                                                     tiler_cuda_status* st) {
   __shared__ float red[kQThreads / 32];
-  __shared__ unsigned long long nan_at[kQThreads / 32];
+  __shared__ uint32_t nan_at[kQThreads / 32];
   const uint64_t row = blockIdx.x;
   const float* xr = x + row * extent;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool vec = (extent % 4 == 0) && ((uintptr_t)x % 16 == 0);
   float m = 0.0f;
-  unsigned long long first_nan = ~0ull;
+  uint32_t first_nan = 0xffffffffu;  // column of the first NaN (extent < 2^32)
   if (vec) {
     const float4* x4 = reinterpret_cast<const float4*>(xr);
-    for (uint64_t v = threadIdx.x; v < extent / 4; v += kQThreads) {
+    for (uint32_t v = threadIdx.x; v < (uint32_t)(extent / 4); v += kQThreads) {
       const float4 q = __ldg(x4 + v);
       const float e[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        if (isnan(e[j]) && first_nan == ~0ull) first_nan = v * 4 + j;
+        const uint32_t col = v * 4 + j;
+        if (is_nan_bits(e[j])) first_nan = col < first_nan ? col : first_nan;
         m = maximum(m, fabsf(e[j]));
       }
     }
   } else {
-    for (uint64_t i = threadIdx.x; i < extent; i += kQThreads) {
+    for (uint32_t i = threadIdx.x; i < (uint32_t)extent; i += kQThreads) {
       const float e = xr[i];
-      if (isnan(e) && first_nan == ~0ull) first_nan = i;
+      if (is_nan_bits(e)) first_nan = i < first_nan ? i : first_nan;
       m = maximum(m, fabsf(e));
     }
   }
 #pragma unroll
   for (int k = 1; k < 32; k <<= 1) {
     m = maximum(m, __shfl_xor_sync(0xffffffffu, m, k));
-    first_nan = min(first_nan, (unsigned long long)__shfl_xor_sync(0xffffffffu, first_nan, k));
+    const uint32_t o = __shfl_xor_sync(0xffffffffu, first_nan, k);
+    first_nan = o < first_nan ? o : first_nan;
   }
   if (lane == 0) { red[warp] = m; nan_at[warp] = first_nan; }
   __syncthreads();
   m = red[0];
   first_nan = nan_at[0];
-  for (int i = 1; i < kQThreads / 32; ++i) { m = maximum(m, red[i]); first_nan = min(first_nan, nan_at[i]); }
-  if (first_nan != ~0ull) {
+  for (int i = 1; i < kQThreads / 32; ++i) {
+    m = maximum(m, red[i]);
+    first_nan = nan_at[i] < first_nan ? nan_at[i] : first_nan;
+  }
+  if (first_nan != 0xffffffffu) {
     if (threadIdx.x == 0) report_error(st, row * extent + first_nan, TILER_CUDA_NAN_INPUT);
     return;
   }
   // maximum|x| over a NaN-free row; 0 stays +0 (all |x| are non-negative)
   const float scale = __fdiv_rn(m, 127.0f);
   if (threadIdx.x == 0) scales[row] = scale;
-  if (!(isnormal(scale) && scale > 0.0f)) {
+  if (!is_positive_normal(scale)) {
     if (threadIdx.x == 0) report_error(st, row * extent, TILER_CUDA_SCALE_DOMAIN);
     return;
   }

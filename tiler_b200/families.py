@@ -134,7 +134,7 @@ def grouped_workspace(rows: int, grouping: dict, device=None) -> torch.Tensor:
 
 def _reduce(fn_name: str, x: torch.Tensor, grouping, workspace):
     assert x.dtype == torch.float32
-    rows = 1 if x.dim() <= 1 else x.numel() // x.shape[-1]
+    rows = _rows(x)
     count = x.numel() if x.dim() <= 1 else x.shape[-1]
     if grouping is None:
         grouping = plan_grouping(rows, count) if count else {"partitions": 1, "threads": 32, "k": 1, "rounds": 1}
@@ -159,9 +159,18 @@ def max_f32(x: torch.Tensor, grouping: dict | None = None, workspace=None) -> to
     return _reduce("tiler_cuda_max_f32", x, grouping, workspace)
 
 
+def _rows(x: torch.Tensor) -> int:
+    if x.dim() <= 1:
+        return 1
+    r = 1
+    for d in x.shape[:-1]:
+        r *= d
+    return r
+
+
 def strict_sum_f32(x: torch.Tensor) -> torch.Tensor:
     """strict_sum (evaluate.rs:498-589): one serial fold per row."""
-    rows = 1 if x.dim() <= 1 else x.numel() // x.shape[-1]
+    rows = _rows(x)
     count = x.numel() if x.dim() <= 1 else x.shape[-1]
     out = torch.empty(rows, dtype=torch.float32, device=x.device)
     _check(N.lib().tiler_cuda_strict_sum_f32(context(), _stream(), _ptr(x), rows, count, _ptr(out)), "strict_sum")
@@ -170,7 +179,7 @@ def strict_sum_f32(x: torch.Tensor) -> torch.Tensor:
 
 def partitioned_sum_f32(x: torch.Tensor, partitions: int, per_partition: int) -> torch.Tensor:
     """strict_partitioned_sum (evaluate.rs:749-832)."""
-    rows = 1 if x.dim() <= 1 else x.numel() // x.shape[-1]
+    rows = _rows(x)
     count = x.numel() if x.dim() <= 1 else x.shape[-1]
     ws = torch.empty(max(1, rows * partitions), dtype=torch.float32, device=x.device)
     out = torch.empty(rows, dtype=torch.float32, device=x.device)
@@ -183,7 +192,7 @@ def partitioned_sum_f32(x: torch.Tensor, partitions: int, per_partition: int) ->
 def cooperative_sum_f32(x: torch.Tensor, participants: int, per_partition: int, rounds: int,
                         participant_major: bool = False) -> torch.Tensor:
     """cooperative_grouped_sum (evaluate.rs:936-1158)."""
-    rows = 1 if x.dim() <= 1 else x.numel() // x.shape[-1]
+    rows = _rows(x)
     count = x.numel() if x.dim() <= 1 else x.shape[-1]
     out = torch.empty(rows, dtype=torch.float32, device=x.device)
     _check(N.lib().tiler_cuda_cooperative_sum_f32(context(), _stream(), _ptr(x), rows, count, participants,
@@ -298,7 +307,10 @@ def silu(x: torch.Tensor, check=True) -> torch.Tensor:
 
 def scale_bias(x: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """multiply-f32 then add-f32 (standard.rs:105-120): y = (x*a)+b, two
-    roundings; a rank-0 ``a``/``b`` broadcasts."""
+    roundings; a rank-0 ``a``/``b`` broadcasts, otherwise it has x's size."""
+    for t in (a, b):
+        if t.dim() != 0 and t.numel() != x.numel():
+            raise ValueError("scale_bias operands are rank-0 or the size of x")
     y = torch.empty_like(x)
     _check(N.lib().tiler_cuda_scale_bias_f32(context(), _stream(), _ptr(x), x.numel(), _ptr(a), int(a.dim() == 0),
                                              _ptr(b), int(b.dim() == 0), _ptr(y)), "scale_bias")
