@@ -424,14 +424,17 @@ int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t caus
                                                                                        causal_period, row_offset, y, st);
     return 0;
   }
-  const size_t smem = 2048 + 128 + (size_t)kSmxWarps * extent * 4;
+  // Warps per CTA: up to 8, each holding one row (extent*4 bytes) in shared
+  // memory, within what one CTA may use.
+  const size_t fixed = 2048 + 128, row_bytes = extent * 4;
+  const unsigned wpb = (unsigned)umin64(kSmxWarps, (220 * 1024 - fixed) / row_bytes);
+  const size_t smem = fixed + (size_t)wpb * row_bytes;
   cudaFuncSetAttribute(softmax_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  int per_sm = 1;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, softmax_staged_kernel, kSmxWarps * 32, smem);
-  per_sm = std::max(per_sm, 1);
-  const uint64_t want = (rows + kSmxWarps - 1) / kSmxWarps;
+  // CTAs per SM that fit the SM's shared memory (228 KB, 1 KB reserved per CTA).
+  const int per_sm = std::max<int>(1, (int)((228 * 1024) / (smem + 1024)));
+  const uint64_t want = (rows + wpb - 1) / wpb;
   const unsigned grid = (unsigned)umin64(want, (uint64_t)sm_count * per_sm);
-  softmax_staged_kernel<<<grid, kSmxWarps * 32, smem, stream>>>(x, rows, extent, causal_period, row_offset, y, st);
+  softmax_staged_kernel<<<grid, wpb * 32, smem, stream>>>(x, rows, extent, causal_period, row_offset, y, st);
   return 0;
 }
 
