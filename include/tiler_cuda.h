@@ -174,6 +174,17 @@ int32_t tiler_cuda_sum_f32(tiler_cuda_context* ctx, void* stream, const float* x
 int32_t tiler_cuda_max_f32(tiler_cuda_context* ctx, void* stream, const float* x, uint64_t rows,
                            uint64_t count, const tiler_cuda_grouping* g, void* workspace,
                            uint64_t workspace_bytes, float* out);
+/* No counterpart in the reference.  The grouped sum above for callers that
+ * cannot allocate device memory (a host framework that plans every buffer
+ * itself, a loop that must not call cudaMalloc): the partials and tickets
+ * live in a fixed array inside the library (about 260 KB on every GPU that
+ * loads it, kept until the process exits) instead of a caller workspace.
+ * Limits: rows <= 1024 and rows * partitions <= 65536, else
+ * TILER_CUDA_SHAPE_TOO_LARGE.  The first call on a device looks up the
+ * array's device address (make it before any stream capture); calls that
+ * overlap on the GPU share the array and race.  Allocates nothing. */
+int32_t tiler_cuda_sum_f32_no_alloc(tiler_cuda_context* ctx, void* stream, const float* x, uint64_t rows,
+                                    uint64_t count, const tiler_cuda_grouping* g, float* out);
 /* strict_sum, evaluate.rs:498-589 (one serial fold per row). */
 int32_t tiler_cuda_strict_sum_f32(tiler_cuda_context* ctx, void* stream, const float* x,
                                   uint64_t rows, uint64_t count, float* out);

@@ -85,6 +85,7 @@ SIGNATURES = {
     "tiler_cuda_grouped_workspace_bytes": (u64, [u64, C.POINTER(Grouping)]),
     "tiler_cuda_sum_f32": (i32, [P, P, P, u64, u64, C.POINTER(Grouping), P, u64, P]),
     "tiler_cuda_max_f32": (i32, [P, P, P, u64, u64, C.POINTER(Grouping), P, u64, P]),
+    "tiler_cuda_sum_f32_no_alloc": (i32, [P, P, P, u64, u64, C.POINTER(Grouping), P]),
     "tiler_cuda_strict_sum_f32": (i32, [P, P, P, u64, u64, P]),
     "tiler_cuda_partitioned_sum_f32": (i32, [P, P, P, u64, u64, u64, u64, P, u64, P]),
     "tiler_cuda_partitioned_workspace_bytes": (u64, [u64, u64]),

@@ -6,3 +6,4 @@
 #include "maps.cu"
 #include "gemm.cu"
 #include "abi.cu"
+#include "no_alloc.cu"
