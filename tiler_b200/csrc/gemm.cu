@@ -18,9 +18,8 @@
 //                 stores; accumulator b of tile i+1 fills while tile i drains.
 //    Every mbarrier wait is bounded; a wait that gives up records a timeout
 //    in the status word and the CTA stops, frees its TMEM and returns.
-#include <cuda.h>
-
 #include "common.cuh"
+#include "tmap.cuh"
 #include "kernels.h"
 
 namespace tc {
@@ -243,33 +242,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)p;
-  }
-  return fn;
-}
-
 // K-major bf16 matrix [rows, k] -> tensor map with a (64 x box_rows) box.
 static bool make_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k, uint32_t box_rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {k, rows};
-  cuuint64_t strides[1] = {k * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return make_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, k, rows, k * 2, (uint32_t)kBK, box_rows,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k, int epilogue,

@@ -10,6 +10,7 @@
 // one write per element.
 #include "common.cuh"
 #include "kernels.h"
+#include "tmap.cuh"
 
 namespace tc {
 
@@ -17,33 +18,76 @@ namespace tc {
 // RMS normalization
 // ---------------------------------------------------------------------------
 //
-// Per CTA: a contiguous block of rows, processed in groups of up to GR (<= 32)
-// rows.  Warp 0 (one elected lane) streams 256-byte row chunks of the group
-// into a ring of shared-memory stages with cp.async.bulk (one mbarrier per
-// stage, loads marked L2 evict_last); warp 1 is the chain warp, lane r folding
-// row r's squares strictly from the staged chunks; once a group's scales are
-// known (mean = total/N, t = mean + eps, correctly rounded 1/sqrt(t)) the
-// normalize warps re-read the group's rows (an L2 hit: the rows were loaded a
-// few microseconds earlier; read with evict_first) and write y = w*(x*s) with
-// streaming stores, while the producer and the chain warp already work on
-// the next group.
+// Per CTA (one per SM): a contiguous block of rows, split into waves of up to
+// kRmsWave rows.  The CTA runs kRmsPipes independent pipelines; pipeline p
+// takes waves p, p + kRmsPipes, ... and pipeline p > 0 starts when pipeline
+// p-1 has folded half of its first wave, so the pipelines' load, fold and
+// store phases interleave instead of hitting HBM and L2 all at once.
+//
+// One pipeline = 2 producer warps + 1 chain warp + kRmsNormWarps warps:
+//   producers  stream the wave's rows through a ring of shared-memory stages
+//              with 16-byte cp.async copies (completion on the stage's
+//              mbarrier); a stage is one 1 KB column slab of every row of the
+//              wave, rows padded by 16 bytes so the chain lanes' 16-byte reads
+//              down a column are bank-conflict-free;
+//   chain      lane r folds row r's squares strictly in column order
+//              (rms_norm.rs:147-170), loading 8 vectors ahead of the adds;
+//   normalize  once the wave's scales are known (mean = total/N, t = mean +
+//              eps, correctly rounded 1/sqrt(t)), re-read the wave's rows (an
+//              L2 hit, evict_first) and write y = w*(x*s) with streaming
+//              stores, while the producers and the chain move on.
 
-constexpr int kRmsChunkBytes = 256;
-constexpr int kRmsPitch = kRmsChunkBytes + 16;  // conflict-free float4 reads down a column of rows
-constexpr int kRmsStages = 8;
-constexpr int kRmsMaxGroup = 32;
-constexpr int kRmsNormWarps = 6;
-constexpr int kRmsThreads = 32 * (2 + kRmsNormWarps);
+#ifndef TILER_RMS_WAVE
+#define TILER_RMS_WAVE 28
+#endif
+#ifndef TILER_RMS_STAGES
+#define TILER_RMS_STAGES 5
+#endif
+#ifndef TILER_RMS_PIPES
+#define TILER_RMS_PIPES 1
+#endif
+#ifndef TILER_RMS_NORM_WARPS
+#define TILER_RMS_NORM_WARPS 10
+#endif
+#ifndef TILER_RMS_SLAB
+#define TILER_RMS_SLAB 1024
+#endif
+constexpr int kRmsSlabBytes = TILER_RMS_SLAB;
+constexpr int kRmsPitch = kRmsSlabBytes + 16;
+constexpr int kRmsWave = TILER_RMS_WAVE;  // rows per wave (one chain lane per row), <= 32
+constexpr int kRmsStages = TILER_RMS_STAGES;
+constexpr int kRmsPipes = TILER_RMS_PIPES;
+constexpr int kRmsLoadWarps = 2;
+constexpr int kRmsNormWarps = TILER_RMS_NORM_WARPS;
+constexpr int kRmsPipeWarps = kRmsLoadWarps + 1 + kRmsNormWarps;
+constexpr int kRmsThreads = 32 * kRmsPipeWarps * kRmsPipes;
 
-struct RmsSmem {
-  alignas(128) uint8_t stage[kRmsStages][kRmsMaxGroup][kRmsPitch];
+struct RmsPipeSmem {
+  alignas(128) uint8_t stage[kRmsStages][kRmsWave * kRmsPitch];
   uint64_t full[kRmsStages];
   uint64_t empty[kRmsStages];
   uint64_t scale_full[2];
   uint64_t scale_empty[2];
-  float scale[2][kRmsMaxGroup];
+  uint64_t started;  // arrived once this pipeline has folded half of its first wave
+  float scale[2][kRmsWave];
+};
+struct RmsSmem {
+  RmsPipeSmem pipe[kRmsPipes];
   int abort;
 };
+constexpr size_t kRmsSmemBytes = sizeof(RmsSmem);
+
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ uint4 lds_u4_nv(uint32_t saddr) {
+  uint4 v;
+  asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr));
+  return v;
+}
 
 template <bool BF16>
 struct RmsElem;
@@ -86,127 +130,169 @@ __device__ __forceinline__ uint4 ld_u4_policy(const void* p, uint64_t policy) {
   return v;
 }
 
+// Folds `n` 16-byte vectors of one staged row into acc (strict order).
+template <class E>
+__device__ __forceinline__ float rms_fold_vectors(float acc, uint32_t rowp, uint32_t v, uint32_t n) {
+  constexpr uint32_t B = 8;
+  for (; v + B <= n; v += B) {
+    uint4 q[B];
+#pragma unroll
+    for (uint32_t b = 0; b < B; ++b) q[b] = lds_u4_nv(rowp + (v + b) * 16);
+#pragma unroll
+    for (uint32_t b = 0; b < B; ++b) {
+      float e[E::kPerVec];
+      E::unpack(q[b], e);
+#pragma unroll
+      for (int j = 0; j < E::kPerVec; ++j) acc = __fadd_rn(acc, __fmul_rn(e[j], e[j]));
+    }
+  }
+  for (; v < n; ++v) {
+    float e[E::kPerVec];
+    E::unpack(lds_u4_nv(rowp + v * 16), e);
+#pragma unroll
+    for (int j = 0; j < E::kPerVec; ++j) acc = __fadd_rn(acc, __fmul_rn(e[j], e[j]));
+  }
+  return acc;
+}
+
 template <bool BF16>
-__global__ void __launch_bounds__(kRmsThreads) rms_norm_kernel(const uint8_t* __restrict__ x,
-                                                              const uint8_t* __restrict__ w, int64_t w_row_stride,
-                                                              uint64_t rows, uint64_t extent, float eps,
-                                                              uint8_t* __restrict__ y, uint32_t group_rows,
-                                                              tiler_cuda_status* st) {
+__global__ void __launch_bounds__(kRmsThreads, 1)
+    rms_norm_kernel(const uint8_t* __restrict__ x, const uint8_t* __restrict__ w, int64_t w_row_stride,
+                    uint64_t rows, uint64_t extent, float eps, uint8_t* __restrict__ y, uint32_t wave_rows,
+                    tiler_cuda_status* st) {
   using E = RmsElem<BF16>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  RmsSmem& S = *reinterpret_cast<RmsSmem*>(smem_raw);
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  RmsSmem& SS = *reinterpret_cast<RmsSmem*>(smem_raw);
+  const uint32_t pipe = threadIdx.x / (32 * kRmsPipeWarps);
+  const uint32_t pwarp = (threadIdx.x / 32) % kRmsPipeWarps, lane = threadIdx.x & 31;
+  RmsPipeSmem& S = SS.pipe[pipe];
   const uint64_t esize = sizeof(typename E::T);
   const uint64_t row_bytes = extent * esize;
   const uint64_t rb = blockIdx.x * rows / gridDim.x, re = (blockIdx.x + 1) * rows / gridDim.x;
   const uint64_t my_rows = re - rb;
-  const uint32_t GR = group_rows;
-  const uint64_t ngroups = (my_rows + GR - 1) / GR;
-  const uint64_t nchunks = (row_bytes + kRmsChunkBytes - 1) / kRmsChunkBytes;
-  const uint64_t total = ngroups * nchunks;
+  const uint32_t WR = wave_rows;
+  const uint64_t nwaves_all = (my_rows + WR - 1) / WR;
+  // this pipeline's waves: pipe, pipe + kRmsPipes, ...
+  const uint64_t nwaves = nwaves_all > pipe ? (nwaves_all - pipe + kRmsPipes - 1) / kRmsPipes : 0;
+  const uint64_t nslabs = (row_bytes + kRmsSlabBytes - 1) / kRmsSlabBytes;
+  const uint64_t total = nwaves * nslabs;
+  auto wave_first_row = [&](uint64_t wv) { return (pipe + wv * kRmsPipes) * (uint64_t)WR; };
+  auto wave_rows_of = [&](uint64_t wv) { return (uint32_t)umin64(WR, my_rows - wave_first_row(wv)); };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRmsStages; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&S.scale_full[s], 1); mbar_init(&S.scale_empty[s], kRmsNormWarps); }
-    S.abort = 0;
+    for (int p = 0; p < kRmsPipes; ++p) {
+      RmsPipeSmem& Q = SS.pipe[p];
+      for (int s = 0; s < kRmsStages; ++s) { mbar_init(&Q.full[s], kRmsLoadWarps * 32); mbar_init(&Q.empty[s], 1); }
+      for (int s = 0; s < 2; ++s) { mbar_init(&Q.scale_full[s], 1); mbar_init(&Q.scale_empty[s], kRmsNormWarps); }
+      mbar_init(&Q.started, 1);
+    }
+    SS.abort = 0;
     fence_barrier_init();
   }
   __syncthreads();
-  if (ngroups == 0) return;
+  volatile int* abort_flag = &SS.abort;
+  if (nwaves == 0) return;
 
-  if (warp == 0) {
-    // ---- producer: one lane issues every bulk copy --------------------------
-    if (lane == 0) {
-      const uint64_t keep = policy_evict_last();
-      for (uint64_t i = 0; i < total; ++i) {
-        const uint32_t stage = i % kRmsStages;
-        const uint64_t use = i / kRmsStages;
-        if (use > 0 && !mbar_wait(&S.empty[stage], (uint32_t)((use - 1) & 1), st)) { S.abort = 1; break; }
-        if (*(volatile int*)&S.abort) break;
-        const uint64_t g = i / nchunks, c = i % nchunks;
-        const uint32_t gr = (uint32_t)umin64(GR, my_rows - g * GR);
-        const uint32_t bytes = (uint32_t)umin64(kRmsChunkBytes, row_bytes - c * kRmsChunkBytes);
-        mbar_arrive_expect_tx(&S.full[stage], gr * bytes);
-        for (uint32_t r = 0; r < gr; ++r) {
-          const uint8_t* src = x + (rb + g * GR + r) * row_bytes + c * kRmsChunkBytes;
-          bulk_g2s(&S.stage[stage][r][0], src, bytes, &S.full[stage], keep);
-        }
+  if (pwarp < kRmsLoadWarps) {
+    // ---- producers -----------------------------------------------------------
+    const uint32_t t = threadIdx.x % (32 * kRmsPipeWarps);
+    if (pipe > 0 && !mbar_wait(&SS.pipe[pipe - 1].started, 0, st))
+      *abort_flag = 1;
+    for (uint64_t i = 0; i < total && !*abort_flag; ++i) {
+      const uint32_t stage = i % kRmsStages;
+      const uint64_t use = i / kRmsStages;
+      if (use > 0 && !mbar_wait(&S.empty[stage], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
+      const uint64_t wv = i / nslabs, c = i % nslabs;
+      const uint32_t wr = wave_rows_of(wv);
+      const uint32_t chunks = (uint32_t)umin64(kRmsSlabBytes, row_bytes - c * kRmsSlabBytes) / 16;
+      const uint32_t sbase = smem_u32(&S.stage[stage][0]);
+      const uint8_t* gbase = x + (rb + wave_first_row(wv)) * row_bytes + c * kRmsSlabBytes;
+      for (uint32_t q = t; q < wr * (kRmsSlabBytes / 16); q += kRmsLoadWarps * 32) {
+        const uint32_t r = q / (kRmsSlabBytes / 16), c16 = q % (kRmsSlabBytes / 16);
+        if (c16 < chunks) cp_async16(sbase + r * kRmsPitch + c16 * 16, gbase + r * row_bytes + c16 * 16);
       }
+      cp_async_arrive(&S.full[stage]);
     }
-  } else if (warp == 1) {
-    // ---- chain warp: lane r folds row r's squares in order -------------------
-    for (uint64_t g = 0; g < ngroups; ++g) {
-      const uint32_t gr = (uint32_t)umin64(GR, my_rows - g * GR);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (pwarp == kRmsLoadWarps) {
+    // ---- chain warp ------------------------------------------------------------
+    bool signalled = false;
+    for (uint64_t wv = 0; wv < nwaves; ++wv) {
+      const uint32_t wr = wave_rows_of(wv);
       float acc = 0.0f;
-      bool first = true;
-      for (uint64_t c = 0; c < nchunks; ++c) {
-        const uint64_t i = g * nchunks + c;
+      for (uint64_t c = 0; c < nslabs; ++c) {
+        const uint64_t i = wv * nslabs + c;
         const uint32_t stage = i % kRmsStages;
-        if (!mbar_wait(&S.full[stage], (uint32_t)((i / kRmsStages) & 1), st)) S.abort = 1;
-        if (*(volatile int*)&S.abort) return;
-        const uint32_t bytes = (uint32_t)umin64(kRmsChunkBytes, row_bytes - c * kRmsChunkBytes);
-        if (lane < gr) {
-          const uint4* src = reinterpret_cast<const uint4*>(&S.stage[stage][lane][0]);
-          const uint32_t nvec = bytes / 16;
-#pragma unroll 4
-          for (uint32_t v = 0; v < nvec; ++v) {
+        if (!mbar_wait(&S.full[stage], (uint32_t)((i / kRmsStages) & 1), st)) *abort_flag = 1;
+        if (*abort_flag) break;
+        const uint32_t nvec = (uint32_t)umin64(kRmsSlabBytes, row_bytes - c * kRmsSlabBytes) / 16;
+#ifndef TILER_RMS_PROBE_NO_CHAIN
+        if (lane < wr) {
+          const uint32_t rowp = smem_u32(&S.stage[stage][lane * kRmsPitch]);
+          uint32_t v = 0;
+          if (c == 0) {  // the fold is seeded at the first square
             float e[E::kPerVec];
-            E::unpack(src[v], e);
+            E::unpack(lds_u4_nv(rowp), e);
+            acc = __fmul_rn(e[0], e[0]);
 #pragma unroll
-            for (int j = 0; j < E::kPerVec; ++j) {
-              const float sq = __fmul_rn(e[j], e[j]);
-              acc = first ? sq : __fadd_rn(acc, sq);
-              first = false;
-            }
+            for (int j = 1; j < E::kPerVec; ++j) acc = __fadd_rn(acc, __fmul_rn(e[j], e[j]));
+            v = 1;
           }
+          acc = rms_fold_vectors<E>(acc, rowp, v, nvec);
         }
+#endif
         __syncwarp();
-        if (lane == 0) mbar_arrive(&S.empty[stage]);
+        if (lane == 0) {
+          mbar_arrive(&S.empty[stage]);
+          if (!signalled && (c + 1) * 2 >= nslabs) { mbar_arrive(&S.started); signalled = true; }
+        }
       }
+      if (*abort_flag) break;
       // rms_norm.rs:172-193: mean = total / N, t = mean + eps, certified rsqrt
       const float mean = __fdiv_rn(acc, (float)extent);
       const float s = rsqrt_cr(__fadd_rn(mean, eps));
-      const uint32_t slot = g & 1;
-      const uint64_t use = g >> 1;
-      if (use > 0 && !mbar_wait(&S.scale_empty[slot], (uint32_t)((use - 1) & 1), st)) S.abort = 1;
-      if (*(volatile int*)&S.abort) return;
-      if (lane < gr) S.scale[slot][lane] = s;
+      const uint32_t slot = wv & 1;
+      const uint64_t use = wv >> 1;
+      if (use > 0 && !mbar_wait(&S.scale_empty[slot], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
+      if (lane < wr) S.scale[slot][lane] = s;
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.scale_full[slot]);
     }
   } else {
     // ---- normalize warps: y = w * (x * s), two roundings (rms_norm.rs:479-485)
-    const uint32_t nw = warp - 2;
+    const uint32_t nw = pwarp - kRmsLoadWarps - 1;
     const uint64_t drop = policy_evict_first();
     const uint64_t nvec = row_bytes / 16;
-    for (uint64_t g = 0; g < ngroups; ++g) {
-      const uint32_t gr = (uint32_t)umin64(GR, my_rows - g * GR);
-      const uint32_t slot = g & 1;
-      if (!mbar_wait(&S.scale_full[slot], (uint32_t)((g >> 1) & 1), st)) S.abort = 1;
-      if (*(volatile int*)&S.abort) return;
-      for (uint32_t r = nw; r < gr; r += kRmsNormWarps) {
+    for (uint64_t wv = 0; wv < nwaves; ++wv) {
+      const uint32_t wr = wave_rows_of(wv);
+      const uint32_t slot = wv & 1;
+      if (!mbar_wait(&S.scale_full[slot], (uint32_t)((wv >> 1) & 1), st)) *abort_flag = 1;
+      if (*abort_flag) break;
+#ifndef TILER_RMS_PROBE_SKIP_NORMALIZE
+      for (uint32_t r = nw; r < wr; r += kRmsNormWarps) {
         const float s = S.scale[slot][r];
-        const uint64_t row = rb + g * GR + r;
+        const uint64_t row = rb + wave_first_row(wv) + r;
         const uint8_t* xr = x + row * row_bytes;
-        const uint8_t* wr = w + (int64_t)row * w_row_stride * (int64_t)esize;
+        const uint8_t* wrow = w + (int64_t)row * w_row_stride * (int64_t)esize;
         uint8_t* yr = y + row * row_bytes;
-        for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * 4) {
-          uint4 xv[4], wv[4];
+        constexpr int U = 8;  // 16-byte loads in flight per lane
+        for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * U) {
+          uint4 xv[U], wvv[U];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < U; ++u) {
             const uint64_t v = v0 + 32 * u;
             if (v < nvec) {
               xv[u] = ld_u4_policy(xr + v * 16, drop);
-              wv[u] = __ldg(reinterpret_cast<const uint4*>(wr + v * 16));
+              wvv[u] = __ldg(reinterpret_cast<const uint4*>(wrow + v * 16));
             }
           }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
+          for (int u = 0; u < U; ++u) {
             const uint64_t v = v0 + 32 * u;
             if (v < nvec) {
               float xe[E::kPerVec], we[E::kPerVec], ye[E::kPerVec];
               E::unpack(xv[u], xe);
-              E::unpack(wv[u], we);
+              E::unpack(wvv[u], we);
 #pragma unroll
               for (int j = 0; j < E::kPerVec; ++j) ye[j] = canon(__fmul_rn(we[j], __fmul_rn(xe[j], s)));
               st_global_stream_u4(reinterpret_cast<uint4*>(yr + v * 16), E::pack(ye));
@@ -214,6 +300,7 @@ __global__ void __launch_bounds__(kRmsThreads) rms_norm_kernel(const uint8_t* __
           }
         }
       }
+#endif
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.scale_empty[slot]);
     }
@@ -268,20 +355,17 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
       rms_norm_generic_kernel<false><<<blocks, wpb * 32, 0, stream>>>(x, w, w_row_stride, rows, extent, eps, y);
     return 0;
   }
-  // One CTA per SM; each takes rows/grid consecutive rows in groups of GR.
+  // One CTA per SM; each takes rows/grid consecutive rows in waves.
   const uint64_t grid = umin64((uint64_t)sm_count, rows);
-  const uint64_t per_cta = (rows + grid - 1) / grid;
-  uint32_t gr = 16;
-  if (per_cta < gr) gr = (uint32_t)per_cta;
-  const size_t smem = sizeof(RmsSmem);
+  const uint32_t wave = (uint32_t)kRmsWave;
   if (bf16) {
-    cudaFuncSetAttribute(rms_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    rms_norm_kernel<true><<<(unsigned)grid, kRmsThreads, smem, stream>>>(
-        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, gr, st);
+    cudaFuncSetAttribute(rms_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
+    rms_norm_kernel<true><<<(unsigned)grid, kRmsThreads, kRmsSmemBytes, stream>>>(
+        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, wave, st);
   } else {
-    cudaFuncSetAttribute(rms_norm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    rms_norm_kernel<false><<<(unsigned)grid, kRmsThreads, smem, stream>>>(
-        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, gr, st);
+    cudaFuncSetAttribute(rms_norm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
+    rms_norm_kernel<false><<<(unsigned)grid, kRmsThreads, kRmsSmemBytes, stream>>>(
+        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, wave, st);
   }
   return 0;
 }
