@@ -109,7 +109,7 @@ const Entry kEntries[] = {
     {"tiler_cuda.sum_f32.cooperative", (const void*)cooperative_sum_kernel, 1024, 0},
     {"tiler_cuda.rms_norm_f32", (const void*)rms_norm_kernel<false>, kRmsThreads, kRmsSmemBytes},
     {"tiler_cuda.rms_norm_bf16", (const void*)rms_norm_kernel<true>, kRmsThreads, kRmsSmemBytes},
-    {"tiler_cuda.softmax_f32", (const void*)softmax_staged_kernel, kSmxWarps * 32, 2048 + 128 + kSmxWarps * 2048 * 4},
+    {"tiler_cuda.softmax_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.quantize_i8_rows", (const void*)quantize_i8_rows_kernel, kQThreads, 0},
     {"tiler_cuda.dequantize_i8_rows", (const void*)dequantize_i8_rows_kernel, 256, 0},
     {"tiler_cuda.quantize_affine_u8", (const void*)quantize_affine_u8_kernel, 256, 0},

@@ -227,6 +227,34 @@ __device__ __forceinline__ float exp_cr(float x, const double* table_hi, tiler_c
   return f;
 }
 
+// Fast form of exp_cr for a finite argument in (-104, 89): the same Tang
+// evaluation, with n taken by adding 1.5*2^52 (round to nearest in the
+// addition) and the midpoint test done on the bits of the binary64 value:
+// its 29 bits below binary32 precision must differ from the midpoint pattern
+// 1 << 28 by more than 64 units (2^-46 relative, against an evaluation error
+// below 2^-51).  Results outside the normal binary32 range, and undecided
+// ones, go to exp_cr.
+constexpr double kRoundShift = 6755399441055744.0;  // 1.5 * 2^52
+__device__ __forceinline__ float exp_cr_fast(float x, const double* table_hi, tiler_cuda_status* st) {
+  const double xd = (double)x;
+  const double t = __fma_rn(xd, kInvLn2x256, kRoundShift);
+  const int n = __double2loint(t);
+  const double nd = __dsub_rn(t, kRoundShift);
+  double r = __fma_rn(-nd, kLn2By256Hi, xd);
+  r = __fma_rn(-nd, kLn2By256Mid, r);
+  double q = __fma_rn(r, 1.0 / 24.0, 1.0 / 6.0);
+  q = __fma_rn(r, q, 0.5);
+  const double p = __fma_rn(__dmul_rn(r, r), q, r);
+  const double tj = table_hi[n & 255];
+  const double y0 = __fma_rn(tj, p, tj);
+  const int hi = __double2hiint(y0) + ((n >> 8) << 20);
+  const int lo = __double2loint(y0);
+  const int d = (int)((uint32_t)lo & 0x1fffffffu) - 0x10000000;
+  const bool ok = hi >= 0x38100000 && hi < 0x47f00000 && (d > 64 || d < -64);
+  if (ok) return __double2float_rn(__hiloint2double(hi, lo));
+  return exp_cr(x, table_hi, st);
+}
+
 // Correctly rounded binary32 1/sqrt(t) (certified_rsqrt_strict,
 // rms_norm.rs:238-293).  The binary64 candidate is checked exactly: f is the
 // correctly rounded value iff mlo^2 t < 1 < mhi^2 t for the midpoints mlo,
@@ -302,6 +330,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");

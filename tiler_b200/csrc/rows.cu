@@ -83,9 +83,11 @@ __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
 __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Shared-memory 16-byte load.  Volatile so the compiler cannot speculate it
+// above the lane predicate that keeps its address inside the allocation.
 __device__ __forceinline__ uint4 lds_u4_nv(uint32_t saddr) {
   uint4 v;
-  asm("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr));
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr));
   return v;
 }
 
@@ -374,97 +376,221 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
 // Softmax (softmax.rs:260-315) with the in-kernel causal block mask.
 // ---------------------------------------------------------------------------
 //
-// One warp per row at a time, the row staged once in shared memory by a bulk
-// copy.  The maximum (order-free) is a lane-parallel fold plus butterfly; the
-// exponentials are written back over the staged row; lane 0 folds the
-// denominator strictly from shared memory; r = 1/d; out = e * r with
-// streaming stores.  Three CTAs of eight warps per SM keep 24 chains in
-// flight per SM.
+// Each CTA owns G row buffers in shared memory (a buffer is one whole row)
+// and walks its block of rows in groups of G:
+//   1. one lane bulk-copies the group's rows in (one mbarrier);
+//   2. warp w takes row w: the row maximum over the unmasked columns
+//      (order-free, NaN-propagating), then e_i = exp(x_i - m) in place
+//      (certified exp); with the causal mask, columns past the diagonal
+//      hold e = +0 exactly (x + -inf = -inf), so they are zero-filled
+//      without evaluating exp, and a masked x that is NaN or +inf (which
+//      makes that e NaN) is recorded as a poisoned row;
+//   3. the chain warp folds all G denominators at once, lane w folding row
+//      w strictly, d = (((e_0 + e_1) + e_2) + ...), up to the diagonal only
+//      (adding +0.0 to a positive running sum is the identity), r = 1/d;
+//   4. warp w writes out_i = e_i * r with streaming stores.
+// Several CTAs share an SM (G is sized so three fit), so one CTA's loads
+// and folds overlap the others' exponentials and stores.
 
-constexpr int kSmxWarps = 8;  // at most; fewer for long rows (shared memory)
+#ifndef TILER_SMX_CTAS_PER_SM
+#define TILER_SMX_CTAS_PER_SM 4
+#endif
+#ifndef TILER_SMX_MAX_GROUP
+#define TILER_SMX_MAX_GROUP 6
+#endif
+constexpr int kSmxMaxGroup = TILER_SMX_MAX_GROUP;  // rows per CTA group
 constexpr uint64_t kSmxMaxExtent = 8192;
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+__global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM)
+    softmax_group_kernel(const float* __restrict__ x, uint64_t rows, uint64_t extent, uint64_t period,
+                         uint64_t row_offset, float* __restrict__ y, uint32_t group, tiler_cuda_status* st) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  double* table = reinterpret_cast<double*>(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + 2048);
+  float* rcp = reinterpret_cast<float*>(smem_raw + 2048 + 16);
+  uint32_t* poisoned = reinterpret_cast<uint32_t*>(smem_raw + 2048 + 16 + 4 * kSmxMaxGroup);
+  float* bufs = reinterpret_cast<float*>(smem_raw + 2048 + 256);
+  // warp 0 folds the denominators (the oldest warp, so the scheduler tends to
+  // favour its dependent chain); warp w + 1 handles row w of each group.
+  const uint32_t lane = threadIdx.x & 31;
+  const bool chain_warp = (threadIdx.x >> 5) == 0;
+  const uint32_t warp = (threadIdx.x >> 5) - 1;  // row index for the row warps
+  const uint32_t G = group;
+  const uint32_t ext = (uint32_t)extent, row_bytes = ext * 4;
+  // Groups are G consecutive rows (similar causal lengths, so the lockstep
+  // fold of a group wastes little); CTA b takes groups b, b + grid, ... so
+  // every CTA gets a mix of short and long groups.
+  const uint64_t total_groups = (rows + G - 1) / G;
+  const uint64_t ngroups = total_groups > blockIdx.x ? (total_groups - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  auto group_row0 = [&](uint64_t g) { return (blockIdx.x + g * (uint64_t)gridDim.x) * G; };
+  const bool causal = period != 0;
+  const uint64_t drop = policy_evict_first();
+
+  load_exp_table(table);
+  if (threadIdx.x == 0) {
+    mbar_init(full, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+#ifdef TILER_SMX_PROBE_SPAN
+  const uint64_t span_t0 = global_ns();
+#endif
+
+  for (uint64_t g = 0; g < ngroups; ++g) {
+    const uint64_t row0 = group_row0(g);
+    const uint32_t n = (uint32_t)umin64(G, rows - row0);
+    if (threadIdx.x == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive_expect_tx(full, n * row_bytes);
+      for (uint32_t r = 0; r < n; ++r)
+        bulk_g2s(bufs + (uint64_t)r * ext, x + (row0 + r) * extent, row_bytes, full, drop);
+    }
+#ifdef TILER_SMX_PROBE_TIMES
+    long long t0 = clock64();
+#endif
+    const bool ok = mbar_wait(full, (uint32_t)(g & 1), st);
+    if (!__syncthreads_and(ok)) return;
+#ifdef TILER_SMX_PROBE_TIMES
+    long long t1 = clock64();
+#endif
+
+    if (!chain_warp && warp < n) {
+      // ---- max and exponentials for row `warp` ---------------------------------
+      const uint64_t row = row0 + warp;
+      const uint32_t live = causal ? (uint32_t)umin64((row_offset + row) % period + 1, extent) : ext;
+      float* b = bufs + (uint64_t)warp * ext;
+      float4* b4 = reinterpret_cast<float4*>(b);
+      float m = __uint_as_float(0xff800000u);
+      const uint32_t live4 = live / 4;
+      for (uint32_t v = lane; v < live4; v += 32) {
+        const float4 q = b4[v];
+        m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
+      }
+      for (uint32_t c = live4 * 4 + lane; c < live; c += 32) m = max_nan(m, b[c]);
+      uint32_t bad = 0;  // a masked x that is NaN or +inf poisons the row
+      const uint32_t mask4 = (live + 3) / 4;  // first whole masked vector
+      auto poison = [](uint32_t xb) { return (uint32_t)(((xb & 0x7fffffffu) > 0x7f800000u) | (xb == 0x7f800000u)); };
+      for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) bad |= poison(__float_as_uint(b[c]));
+      for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) {
+        const uint4 q = reinterpret_cast<const uint4*>(b)[v];
+        bad |= poison(q.x) | poison(q.y) | poison(q.z) | poison(q.w);
+      }
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+      bad = __any_sync(0xffffffffu, bad != 0);
+      // m is -inf only if every unmasked x is -inf: x - m is then NaN
+      auto exp_of = [&](float xv) {
+        const float sh = __fsub_rn(xv, m);
+        return sh > -104.0f ? exp_cr_fast(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
+      };
+      uint32_t v = lane;
+      for (; v + 32 < live4; v += 64) {  // two vectors per lane: eight independent exps
+        const float4 q0 = b4[v], q1 = b4[v + 32];
+        const float4 r0 = make_float4(exp_of(q0.x), exp_of(q0.y), exp_of(q0.z), exp_of(q0.w));
+        const float4 r1 = make_float4(exp_of(q1.x), exp_of(q1.y), exp_of(q1.z), exp_of(q1.w));
+        b4[v] = r0;
+        b4[v + 32] = r1;
+      }
+      if (v < live4) {
+        const float4 q0 = b4[v];
+        b4[v] = make_float4(exp_of(q0.x), exp_of(q0.y), exp_of(q0.z), exp_of(q0.w));
+      }
+      for (uint32_t c = live4 * 4 + lane; c < live; c += 32) b[c] = exp_of(b[c]);
+      for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) b[c] = 0.0f;
+      for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (lane == 0) poisoned[warp] = bad;
+    }
+    __syncthreads();
+#ifdef TILER_SMX_PROBE_TIMES
+    long long t2 = clock64();
+#endif
+
+    if (chain_warp) {
+      // ---- chain warp: lane r folds row r's denominator ------------------------
+      if (lane < n) {
+        const uint64_t row = row0 + lane;
+        const uint32_t live = causal ? (uint32_t)umin64((row_offset + row) % period + 1, extent) : ext;
+        const uint32_t base = smem_u32(bufs + (uint64_t)lane * ext);
+        const float* b = bufs + (uint64_t)lane * ext;
+        float acc = b[0];
+        uint32_t c = 1;
+        for (; c < live && (c & 3); ++c) acc = __fadd_rn(acc, b[c]);
+        const uint32_t nv = (live - c) / 4;
+        uint32_t v = 0;
+        for (; v + 8 <= nv; v += 8) {
+          uint4 q[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) q[k] = lds_u4(base + (c + 4 * (v + k)) * 4);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            acc = __fadd_rn(acc, __uint_as_float(q[k].x));
+            acc = __fadd_rn(acc, __uint_as_float(q[k].y));
+            acc = __fadd_rn(acc, __uint_as_float(q[k].z));
+            acc = __fadd_rn(acc, __uint_as_float(q[k].w));
+          }
+        }
+        for (; v < nv; ++v) {
+          const uint4 q = lds_u4(base + (c + 4 * v) * 4);
+          acc = __fadd_rn(acc, __uint_as_float(q.x));
+          acc = __fadd_rn(acc, __uint_as_float(q.y));
+          acc = __fadd_rn(acc, __uint_as_float(q.z));
+          acc = __fadd_rn(acc, __uint_as_float(q.w));
+        }
+        for (c += 4 * nv; c < live; ++c) acc = __fadd_rn(acc, b[c]);
+        const float r = __fdiv_rn(1.0f, acc);
+        rcp[lane] = (poisoned[lane] || is_nan_bits(r)) ? __uint_as_float(kCanonicalNan) : r;
+      }
+    }
+    __syncthreads();
+#ifdef TILER_SMX_PROBE_TIMES
+    long long t3 = clock64();
+#endif
+
+    if (!chain_warp && warp < n) {
+      // ---- out = e * r (softmax.rs:306-312) -----------------------------------
+      const uint64_t row = row0 + warp;
+      const float r = rcp[warp];
+      const float4* b4 = reinterpret_cast<const float4*>(bufs + (uint64_t)warp * ext);
+      float4* yr = reinterpret_cast<float4*>(y + row * extent);
+      if (is_nan_bits(r)) {
+        const float nanv = __uint_as_float(kCanonicalNan);
+        for (uint32_t v = lane; v < ext / 4; v += 32) st_global_stream(yr + v, make_float4(nanv, nanv, nanv, nanv));
+      } else {
+        // e is finite and >= 0 and r finite: the product is never NaN
+        for (uint32_t v = lane; v < ext / 4; v += 32) {
+          const float4 q = b4[v];
+          st_global_stream(yr + v, make_float4(__fmul_rn(q.x, r), __fmul_rn(q.y, r), __fmul_rn(q.z, r),
+                                               __fmul_rn(q.w, r)));
+        }
+      }
+    }
+    __syncthreads();  // the buffers are reloaded for the next group
+#ifdef TILER_SMX_PROBE_SPAN
+    if (threadIdx.x == 0 && g + 1 == ngroups) {
+      uint64_t* T = reinterpret_cast<uint64_t*>(st) + 8;
+      uint32_t smid;
+      asm("mov.u32 %0, %%smid;" : "=r"(smid));
+      T[blockIdx.x * 3] = span_t0; T[blockIdx.x * 3 + 1] = global_ns(); T[blockIdx.x * 3 + 2] = smid;
+    }
+#endif
+#ifdef TILER_SMX_PROBE_TIMES
+    long long t4 = clock64();
+    if (threadIdx.x == 0 && blockIdx.x == 100 && g < 8) {
+      long long* T = reinterpret_cast<long long*>(st) + 8;  // probe scratch after the status word
+      T[g * 4 + 0] = t1 - t0; T[g * 4 + 1] = t2 - t1; T[g * 4 + 2] = t3 - t2; T[g * 4 + 3] = t4 - t3;
+    }
+#endif
+  }
+}
 
 __device__ __forceinline__ float masked_value(float v, uint64_t col, uint64_t diag, bool causal) {
   return (causal && col > diag) ? __fadd_rn(v, __uint_as_float(0xff800000u)) : v;
-}
-
-__global__ void __launch_bounds__(kSmxWarps * 32) softmax_staged_kernel(const float* __restrict__ x, uint64_t rows,
-                                                                     uint64_t extent, uint64_t period,
-                                                                     uint64_t row_offset, float* __restrict__ y,
-                                                                     tiler_cuda_status* st) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  double* table = reinterpret_cast<double*>(smem_raw);  // 256 doubles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + 2048);
-  float* bufs = reinterpret_cast<float*>(smem_raw + 2048 + 128);
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t wpb = blockDim.x >> 5;
-  load_exp_table(table);
-  if (threadIdx.x < wpb) mbar_init(&bars[threadIdx.x], 1);
-  fence_barrier_init();
-  __syncthreads();
-  float* buf = bufs + warp * extent;
-  float4* buf4 = reinterpret_cast<float4*>(buf);
-  const uint64_t nvec = extent / 4;
-  const bool causal = period != 0;
-  const uint64_t drop = policy_evict_first();
-  uint32_t iter = 0;
-  for (uint64_t row = (uint64_t)blockIdx.x * wpb + warp; row < rows; row += (uint64_t)gridDim.x * wpb, ++iter) {
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bars[warp], (uint32_t)(extent * 4));
-      bulk_g2s(buf, x + row * extent, (uint32_t)(extent * 4), &bars[warp], drop);
-    }
-    if (!mbar_wait(&bars[warp], iter & 1, st)) return;
-    const uint64_t diag = causal ? (row_offset + row) % period : 0;
-    // maximum fold (order-free: any grouping is bit-exact, softmax/tests.rs:118)
-    float m = __uint_as_float(0xff800000u);
-    for (uint64_t v = lane; v < nvec; v += 32) {
-      const float4 q = buf4[v];
-      const uint64_t c = v * 4;
-      m = maximum(m, masked_value(q.x, c, diag, causal));
-      m = maximum(m, masked_value(q.y, c + 1, diag, causal));
-      m = maximum(m, masked_value(q.z, c + 2, diag, causal));
-      m = maximum(m, masked_value(q.w, c + 3, diag, causal));
-    }
-#pragma unroll
-    for (int k = 1; k < 32; k <<= 1) m = maximum(m, __shfl_xor_sync(0xffffffffu, m, k));
-    // e_i = exp(x_i - m), one subtraction rounding then the certified exp
-    for (uint64_t v = lane; v < nvec; v += 32) {
-      float4 q = buf4[v];
-      const uint64_t c = v * 4;
-      q.x = exp_cr(__fsub_rn(masked_value(q.x, c, diag, causal), m), table, st);
-      q.y = exp_cr(__fsub_rn(masked_value(q.y, c + 1, diag, causal), m), table, st);
-      q.z = exp_cr(__fsub_rn(masked_value(q.z, c + 2, diag, causal), m), table, st);
-      q.w = exp_cr(__fsub_rn(masked_value(q.w, c + 3, diag, causal), m), table, st);
-      buf4[v] = q;
-    }
-    __syncwarp();
-    float rcp = 0.0f;
-    if (lane == 0) {
-      float d = buf[0];
-      float4 q = buf4[0];
-      d = __fadd_rn(__fadd_rn(__fadd_rn(d, q.y), q.z), q.w);
-#pragma unroll 8
-      for (uint64_t v = 1; v < nvec; ++v) {
-        q = buf4[v];
-        d = __fadd_rn(d, q.x);
-        d = __fadd_rn(d, q.y);
-        d = __fadd_rn(d, q.z);
-        d = __fadd_rn(d, q.w);
-      }
-      rcp = __fdiv_rn(1.0f, d);
-    }
-    rcp = __shfl_sync(0xffffffffu, rcp, 0);
-    float4* yr = reinterpret_cast<float4*>(y + row * extent);
-    for (uint64_t v = lane; v < nvec; v += 32) {
-      float4 q = buf4[v];
-      q.x = canon(__fmul_rn(q.x, rcp));
-      q.y = canon(__fmul_rn(q.y, rcp));
-      q.z = canon(__fmul_rn(q.z, rcp));
-      q.w = canon(__fmul_rn(q.w, rcp));
-      st_global_stream(yr + v, q);
-    }
-    __syncwarp();  // the buffer is reloaded next iteration
-  }
 }
 
 // Any-shape path: one warp per row, y doubles as the exponential scratch.
@@ -500,25 +626,27 @@ __global__ void softmax_generic_kernel(const float* __restrict__ x, uint64_t row
 int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t causal_period, uint64_t row_offset,
                    float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
   if (rows == 0 || extent == 0) return 0;
+  // G rows per CTA, sized so three CTAs share an SM's shared memory.
+  const size_t fixed = 2048 + 256, row_bytes = extent * 4;
+  const uint64_t g3 = ((224 * 1024) / TILER_SMX_CTAS_PER_SM - 1024 - fixed) / row_bytes;
+  const uint64_t g1 = (220 * 1024 - fixed) / row_bytes;
+  const uint64_t G = umin64(kSmxMaxGroup, umin64(rows, g3 >= 4 ? g3 : g1));
   const bool staged = (extent % 4 == 0) && extent <= kSmxMaxExtent && ((uintptr_t)x % 16 == 0) &&
-                      ((uintptr_t)y % 16 == 0);
+                      ((uintptr_t)y % 16 == 0) && G >= 1;
   if (!staged) {
     const unsigned wpb = 8;
     softmax_generic_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, stream>>>(x, rows, extent,
                                                                                        causal_period, row_offset, y, st);
     return 0;
   }
-  // Warps per CTA: up to 8, each holding one row (extent*4 bytes) in shared
-  // memory, within what one CTA may use.
-  const size_t fixed = 2048 + 128, row_bytes = extent * 4;
-  const unsigned wpb = (unsigned)umin64(kSmxWarps, (220 * 1024 - fixed) / row_bytes);
-  const size_t smem = fixed + (size_t)wpb * row_bytes;
-  cudaFuncSetAttribute(softmax_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  // CTAs per SM that fit the SM's shared memory (228 KB, 1 KB reserved per CTA).
+  const size_t smem = fixed + G * row_bytes;
+  cudaFuncSetAttribute(softmax_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // all of the SM's unified L1/shared storage as shared memory, so three CTAs fit
+  cudaFuncSetAttribute(softmax_group_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   const int per_sm = std::max<int>(1, (int)((228 * 1024) / (smem + 1024)));
-  const uint64_t want = (rows + wpb - 1) / wpb;
-  const unsigned grid = (unsigned)umin64(want, (uint64_t)sm_count * per_sm);
-  softmax_staged_kernel<<<grid, wpb * 32, smem, stream>>>(x, rows, extent, causal_period, row_offset, y, st);
+  const unsigned grid = (unsigned)umin64((rows + G - 1) / G, (uint64_t)sm_count * per_sm);
+  softmax_group_kernel<<<grid, (unsigned)(32 * (G + 1)), smem, stream>>>(x, rows, extent, causal_period,
+                                                                          row_offset, y, (uint32_t)G, st);
   return 0;
 }
 
