@@ -362,3 +362,31 @@ def test_gemm_bf16_full_config_sampled_rows(fam, oracle_lib):
                      for r in rows])
     err = np.abs(got - want) / np.maximum(np.abs(want), 1e-3)
     assert err.max() <= 1e-2, f"max rel err {err.max()}"
+
+
+def test_gemm_silu_epilogue_is_the_bf16_rounding_of_the_certified_silu(fam, oracle_lib):
+    """With one-hot rows of A, each accumulator equals one bf16 value of B
+    exactly, so C = bf16(SiLU(v)) must equal the oracle's rounding of the
+    certified binary32 SiLU bit for bit, across the whole bf16 grid that
+    SiLU maps to finite values."""
+    grid = np.arange(0, 1 << 16, dtype=np.uint32).astype(np.uint16)
+    vals = oracle_lib.bf16_to_f32(grid)
+    keep = grid[np.isfinite(vals) & (np.abs(vals) < 200)]
+    n = 256
+    cols = ((keep.size + n - 1) // n) * n
+    bvals = np.zeros(cols, np.uint16)
+    bvals[:keep.size] = keep
+    k = 64
+    a = np.zeros((128, k), np.uint16)
+    a[np.arange(128), np.arange(128) % k] = oracle_lib.f32_to_bf16(np.ones(1, np.float32))[0]
+    b = np.zeros((cols, k), np.uint16)
+    b[:, 0] = bvals  # only row 0 of A (one-hot at column 0) picks column 0 of B
+    at = cuda(a.view(np.int16)).view(torch.bfloat16)
+    bt = cuda(b.view(np.int16)).view(torch.bfloat16)
+    c = host(fam.gemm_bf16(at, bt, epilogue="silu").view(torch.int16)).view(np.uint16)
+    got = c[0, :keep.size]
+    # the oracle contraction of row 0 (1 * v summed with 0 * 0 terms: -0 becomes +0, as in the reference fold)
+    _, want = oracle_lib.gemm_bf16_silu(a, b, 0, 1, nthreads=8)
+    want = want[0, :keep.size]
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, (bad[:5], keep[bad[:5]], got[bad[:5]], want[bad[:5]])

@@ -295,6 +295,40 @@ __device__ __forceinline__ float silu_cr(float x, const double* table_hi, tiler_
   return canon(__fdiv_rn(x, d));
 }
 
+// SiLU with the fast certified exp: the same value as silu_cr.  For x in
+// (-89, 104) the exponential exp(-x) is finite and above the underflow guard;
+// outside that range silu_cr's guards apply.
+__device__ __forceinline__ float silu_cr_fast(float x, const double* table_hi, tiler_cuda_status* st) {
+  if (x > -89.0f && x < 104.0f) {
+    const float e = exp_cr_fast(-x, table_hi, st);
+    return __fdiv_rn(x, __fadd_rn(1.0f, e));
+  }
+  return silu_cr(x, table_hi, st);
+}
+
+// bf16(SiLU(x)) for the contraction epilogue: the bf16 rounding of the
+// certified binary32 SiLU, without evaluating the certified value in the
+// common case.  An approximation y' = x / (1 + exp(-x)) from the hardware
+// exp2 / fast division has, for |x| < 80, relative error below (|x| + 11) *
+// 2^-24 (argument scaling of exp2 |x| * 2^-24, ex2 2^-22, the add 2^-24,
+// the division 2^-22), i.e. fewer than |x| + 11 binary32 ulps of y.  The bf16
+// rounding of a binary32 value changes only where its low 16 bits cross
+// 0x8000, so when y' sits more than 2|x| + 24 ulps from that point the
+// certified y rounds to the same bf16 as y'.  Otherwise, and outside
+// |x| < 80, the certified path decides.
+__device__ __forceinline__ uint16_t silu_bf16_epilogue(float x, const double* table_hi, tiler_cuda_status* st) {
+  const float ax = fabsf(x);
+  if (ax < 80.0f) {
+    const float e = __expf(-x);
+    const float y = __fdividef(x, __fadd_rn(1.0f, e));
+    const uint32_t b = __float_as_uint(y);
+    const int dist = abs((int)(b & 0xffffu) - 0x8000);
+    const bool normal = ((b >> 23) & 0xffu) != 0;
+    if (normal && (float)dist > 2.0f * ax + 24.0f) return (uint16_t)((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
+  }
+  return f32_to_bf16(silu_cr_fast(x, table_hi, st));
+}
+
 // Copies the 2^(j/256) hi column into shared memory (call by all threads,
 // followed by __syncthreads()).
 __device__ __forceinline__ void load_exp_table(double* smem_table) {

@@ -13,7 +13,8 @@
 //      warp 1     allocates 512 TMEM columns (two 128x256 f32 accumulators)
 //                 and one lane issues tcgen05.mma (kind::f16, M=128, N=256,
 //                 K=16) and tcgen05.commit back to the ring / accumulators;
-//      warps 2-5  epilogue: tcgen05.ld 32 columns at a time, the SiLU of
+//      warps 2-9  epilogue (two per TMEM lane quarter, half the columns each):
+//                 tcgen05.ld 32 columns at a time, the SiLU of
 //                 silu.rs:158-180 (certified exp), RNE to bf16, 16-byte
 //                 stores; accumulator b of tile i+1 fills while tile i drains.
 //    Every mbarrier wait is bounded; a wait that gives up records a timeout
@@ -63,7 +64,8 @@ constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
 constexpr int kTileABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kTileBBytes = kBN * kBK * 2;  // 32 KB
 constexpr int kStageBytes = kTileABytes + kTileBBytes;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmEpiWarps = 8;  // two per TMEM lane quarter, each draining half the columns
+constexpr int kGemmThreads = 32 * (2 + kGemmEpiWarps);
 constexpr uint32_t kTmemCols = 512;
 
 struct GemmBars {
@@ -134,7 +136,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   load_exp_table(table);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(&B.full[s], 1); mbar_init(&B.empty[s], 1); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&B.tmem_full[s], 1); mbar_init(&B.tmem_empty[s], 128); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&B.tmem_full[s], 1); mbar_init(&B.tmem_empty[s], 32 * kGemmEpiWarps); }
     B.abort = 0;
     fence_barrier_init();
   }
@@ -193,8 +195,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // epilogue warps 2..5 -> TMEM lane quarter (warp % 4)
+    // epilogue warps 2..9: TMEM lane quarter (warp % 4), column half (warp - 2) / 4
     const uint32_t quarter = warp & 3;
+    const uint32_t col0 = ((warp - 2) / 4) * (kBN / 2);
     const uint32_t row_in_tile = quarter * 32 + lane;
     uint32_t local = 0;
     for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -206,23 +209,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint64_t row = (uint64_t)mb * kBM + row_in_tile;
       uint16_t* crow = c + row * ldc + (uint64_t)nb * kBN;
 #pragma unroll 1
-      for (uint32_t col = 0; col < (uint32_t)kBN; col += 32) {
+      for (uint32_t col = col0; col < col0 + (uint32_t)kBN / 2; col += 32) {
         uint32_t r[32];
         const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + buf * kBN + col;
         TMEM_LD32(taddr, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         uint32_t packed[16];
+        if (epilogue == 1) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
-          if (epilogue == 1) {
-            v0 = silu_cr(v0, table, st);
-            v1 = silu_cr(v1, table, st);
-          } else {
-            v0 = canon(v0);
-            v1 = canon(v1);
-          }
-          packed[j] = (uint32_t)f32_to_bf16(v0) | ((uint32_t)f32_to_bf16(v1) << 16);
+          for (int j = 0; j < 16; ++j)
+            packed[j] = (uint32_t)silu_bf16_epilogue(__uint_as_float(r[2 * j]), table, st) |
+                        ((uint32_t)silu_bf16_epilogue(__uint_as_float(r[2 * j + 1]), table, st) << 16);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            packed[j] = (uint32_t)f32_to_bf16(canon(__uint_as_float(r[2 * j]))) |
+                        ((uint32_t)f32_to_bf16(canon(__uint_as_float(r[2 * j + 1]))) << 16);
         }
         uint4* dst = reinterpret_cast<uint4*>(crow + col);
 #pragma unroll

@@ -29,10 +29,10 @@ __global__ void silu_kernel(const float* __restrict__ x, uint64_t n, float* __re
     float4* y4 = reinterpret_cast<float4*>(y);
     for (uint64_t v = tid; v < n / 4; v += stride) {
       float4 q = __ldcs(x4 + v);
-      q.x = silu_cr(q.x, table, st);
-      q.y = silu_cr(q.y, table, st);
-      q.z = silu_cr(q.z, table, st);
-      q.w = silu_cr(q.w, table, st);
+      q.x = silu_cr_fast(q.x, table, st);
+      q.y = silu_cr_fast(q.y, table, st);
+      q.z = silu_cr_fast(q.z, table, st);
+      q.w = silu_cr_fast(q.w, table, st);
       st_global_stream(y4 + v, q);
     }
     for (uint64_t i = n / 4 * 4 + tid; i < n; i += stride) y[i] = silu_cr(x[i], table, st);
