@@ -289,7 +289,7 @@ int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, u
   const uint64_t per_round = (uint64_t)T * k;
   // Partitions: an exact divisor of count, aiming at 8 rounds per partition
   // and at least two CTAs per SM across all rows.
-  const uint64_t target_per = per_round * 8;
+  const uint64_t target_per = per_round * 16;
   uint64_t want = std::max<uint64_t>(1, count / target_per);
   const uint64_t min_ctas = 2ull * ctx->facts.sm_count;
   if (rows * want < min_ctas) want = std::max<uint64_t>(want, std::min<uint64_t>(count / per_round, (min_ctas + rows - 1) / rows));
@@ -304,7 +304,7 @@ int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, u
   out->k = k;
   out->rounds = (uint32_t)R;
   if (best >= 64) {
-    const uint32_t k2 = 2;
+    const uint32_t k2 = best >= 1024 ? 4 : 2;
     uint64_t t2 = ((best + k2 - 1) / k2 + 31) / 32 * 32;
     t2 = std::min<uint64_t>(t2, T);
     out->combine_threads = (uint32_t)t2;
@@ -448,7 +448,7 @@ int32_t tiler_cuda_dequantize_i8_rows(tiler_cuda_context* ctx, void* stream, con
                                       const float* scales, uint64_t rows, uint64_t extent, float* y) {
   CHECK_CTX(ctx);
   if (rows == 0 || extent == 0) return TILER_CUDA_OK;
-  if (!codes || !scales || !y) return TILER_CUDA_INVALID_APPLICATION;
+  if (!codes || !scales || !y || rows > 0x7fffffffull) return TILER_CUDA_INVALID_APPLICATION;
   launch_dequantize_i8_rows(codes, scales, rows, extent, y, ctx->facts.sm_count, S(stream));
   return last_error_status();
 }

@@ -673,120 +673,165 @@ __device__ __forceinline__ int8_t code_of(float xv, float scale, float inv) {
   return (int8_t)__float2int_rn(q);
 }
 
-__global__ void __launch_bounds__(kQThreads) quantize_i8_rows_kernel(const float* __restrict__ x, uint64_t extent,
-                                                                    int8_t* __restrict__ codes,
+// Row values are held in registers (up to kQMaxVec float4 per thread, rows of
+// up to 4096 f32 with 256 threads), so x is read from HBM exactly once: all
+// of a thread's loads are issued before the maximum consumes them.
+constexpr int kQMaxVec = 4;
+
+__device__ __forceinline__ void quantize_load_row(const float* xr, uint32_t nvec, float4 (&q)[kQMaxVec]) {
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+#pragma unroll
+  for (int k = 0; k < kQMaxVec; ++k) {
+    const uint32_t v = threadIdx.x + k * kQThreads;
+    q[k] = v < nvec ? __ldcs(x4 + v) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// CTA b codes rows b, b + grid, ... (the launch uses one CTA per row).
+__global__ void __launch_bounds__(kQThreads) quantize_i8_rows_kernel(const float* __restrict__ x, uint64_t rows,
+                                                                    uint64_t extent, int8_t* __restrict__ codes,
                                                                     float* __restrict__ scales,
                                                                     tiler_cuda_status* st) {
-  __shared__ float red[kQThreads / 32];
-  __shared__ uint32_t nan_at[kQThreads / 32];
-  const uint64_t row = blockIdx.x;
-  const float* xr = x + row * extent;
+  __shared__ float red[2][kQThreads / 32];
+  __shared__ uint32_t nan_at[2][kQThreads / 32];
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const bool vec = (extent % 4 == 0) && ((uintptr_t)x % 16 == 0);
-  float m = 0.0f;
-  uint32_t first_nan = 0xffffffffu;  // column of the first NaN (extent < 2^32)
-  if (vec) {
-    const float4* x4 = reinterpret_cast<const float4*>(xr);
-    for (uint32_t v = threadIdx.x; v < (uint32_t)(extent / 4); v += kQThreads) {
-      const float4 q = __ldg(x4 + v);
-      const float e[4] = {q.x, q.y, q.z, q.w};
+  const uint32_t nvec = (uint32_t)(extent / 4);
+  const bool regs = (extent % 4 == 0) && ((uintptr_t)x % 16 == 0) && nvec <= kQMaxVec * kQThreads &&
+                    ((uintptr_t)codes % 4 == 0);
+  float4 q[kQMaxVec], nq[kQMaxVec];
+  uint64_t row = blockIdx.x;
+  if (regs && row < rows) quantize_load_row(x + row * extent, nvec, nq);
+  for (uint32_t it = 0; row < rows; row += gridDim.x, ++it) {
+    const float* xr = x + row * extent;
+    const uint32_t par = it & 1;
+    float m = 0.0f;
+    uint32_t first_nan = 0xffffffffu;  // column of the first NaN (extent < 2^32)
+    if (regs) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t col = v * 4 + j;
-        if (is_nan_bits(e[j])) first_nan = col < first_nan ? col : first_nan;
-        m = maximum(m, fabsf(e[j]));
+      for (int k = 0; k < kQMaxVec; ++k) q[k] = nq[k];
+      if (row + gridDim.x < rows) quantize_load_row(x + (row + gridDim.x) * extent, nvec, nq);
+#pragma unroll
+      for (int k = 0; k < kQMaxVec; ++k) {
+        const uint32_t v = threadIdx.x + k * kQThreads;
+        if (v < nvec) {
+          const float e[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (is_nan_bits(e[j])) first_nan = min(first_nan, v * 4 + j);
+            m = maximum(m, fabsf(e[j]));
+          }
+        }
+      }
+    } else {
+      for (uint32_t i = threadIdx.x; i < (uint32_t)extent; i += kQThreads) {
+        const float e = xr[i];
+        if (is_nan_bits(e)) first_nan = min(first_nan, i);
+        m = maximum(m, fabsf(e));
       }
     }
-  } else {
-    for (uint32_t i = threadIdx.x; i < (uint32_t)extent; i += kQThreads) {
-      const float e = xr[i];
-      if (is_nan_bits(e)) first_nan = i < first_nan ? i : first_nan;
-      m = maximum(m, fabsf(e));
-    }
-  }
 #pragma unroll
-  for (int k = 1; k < 32; k <<= 1) {
-    m = maximum(m, __shfl_xor_sync(0xffffffffu, m, k));
-    const uint32_t o = __shfl_xor_sync(0xffffffffu, first_nan, k);
-    first_nan = o < first_nan ? o : first_nan;
-  }
-  if (lane == 0) { red[warp] = m; nan_at[warp] = first_nan; }
-  __syncthreads();
-  m = red[0];
-  first_nan = nan_at[0];
-  for (int i = 1; i < kQThreads / 32; ++i) {
-    m = maximum(m, red[i]);
-    first_nan = nan_at[i] < first_nan ? nan_at[i] : first_nan;
-  }
-  if (first_nan != 0xffffffffu) {
-    if (threadIdx.x == 0) report_error(st, row * extent + first_nan, TILER_CUDA_NAN_INPUT);
-    return;
-  }
-  // maximum|x| over a NaN-free row; 0 stays +0 (all |x| are non-negative)
-  const float scale = __fdiv_rn(m, 127.0f);
-  if (threadIdx.x == 0) scales[row] = scale;
-  if (!is_positive_normal(scale)) {
-    if (threadIdx.x == 0) report_error(st, row * extent, TILER_CUDA_SCALE_DOMAIN);
-    return;
-  }
-  const float inv = __frcp_rn(scale);
-  int8_t* cr = codes + row * extent;
-  if (vec && ((uintptr_t)codes % 4 == 0)) {
-    const float4* x4 = reinterpret_cast<const float4*>(xr);
-    char4* c4 = reinterpret_cast<char4*>(cr);
-    for (uint64_t v = threadIdx.x; v < extent / 4; v += kQThreads) {
-      const float4 q = __ldg(x4 + v);
-      c4[v] = make_char4(code_of(q.x, scale, inv), code_of(q.y, scale, inv), code_of(q.z, scale, inv),
-                         code_of(q.w, scale, inv));
+    for (int k = 1; k < 32; k <<= 1) {
+      m = maximum(m, __shfl_xor_sync(0xffffffffu, m, k));
+      first_nan = min(first_nan, __shfl_xor_sync(0xffffffffu, first_nan, k));
     }
-  } else {
-    for (uint64_t i = threadIdx.x; i < extent; i += kQThreads) cr[i] = code_of(xr[i], scale, inv);
+    if (lane == 0) { red[par][warp] = m; nan_at[par][warp] = first_nan; }
+    __syncthreads();  // double-buffered slots: the next row writes the other half
+    m = red[par][0];
+    first_nan = nan_at[par][0];
+    for (int i = 1; i < kQThreads / 32; ++i) {
+      m = maximum(m, red[par][i]);
+      first_nan = min(first_nan, nan_at[par][i]);
+    }
+    if (first_nan != 0xffffffffu) {
+      if (threadIdx.x == 0) report_error(st, row * extent + first_nan, TILER_CUDA_NAN_INPUT);
+      continue;
+    }
+    // maximum|x| over a NaN-free row; 0 stays +0 (all |x| are non-negative)
+    const float scale = __fdiv_rn(m, 127.0f);
+    if (threadIdx.x == 0) scales[row] = scale;
+    if (!is_positive_normal(scale)) {
+      if (threadIdx.x == 0) report_error(st, row * extent, TILER_CUDA_SCALE_DOMAIN);
+      continue;
+    }
+    const float inv = __frcp_rn(scale);
+    int8_t* cr = codes + row * extent;
+    if (regs) {
+      char4* c4 = reinterpret_cast<char4*>(cr);
+#pragma unroll
+      for (int k = 0; k < kQMaxVec; ++k) {
+        const uint32_t v = threadIdx.x + k * kQThreads;
+        if (v < nvec)
+          __stcs(reinterpret_cast<int*>(c4 + v),
+                 (int)(uint8_t)code_of(q[k].x, scale, inv) | ((int)(uint8_t)code_of(q[k].y, scale, inv) << 8) |
+                     ((int)(uint8_t)code_of(q[k].z, scale, inv) << 16) |
+                     ((int)(uint8_t)code_of(q[k].w, scale, inv) << 24));
+      }
+    } else {
+      for (uint32_t i = threadIdx.x; i < (uint32_t)extent; i += kQThreads) cr[i] = code_of(xr[i], scale, inv);
+    }
   }
 }
 
 void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
                              tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
-  (void)sm_count;
   if (rows == 0) return;
-  quantize_i8_rows_kernel<<<(unsigned)rows, kQThreads, 0, stream>>>(x, extent, codes, scales, st);
+  (void)sm_count;  // one CTA per row measured fastest (short-lived CTAs keep many rows' loads in flight)
+  const unsigned grid = (unsigned)rows;
+  quantize_i8_rows_kernel<<<grid, kQThreads, 0, stream>>>(x, rows, extent, codes, scales, st);
 }
 
-// dequantize_one with zero point 0 (quantization.rs:440-451).
-__global__ void dequantize_i8_rows_kernel(const int8_t* __restrict__ codes, const float* __restrict__ scales,
-                                          uint64_t rows, uint64_t extent, float* __restrict__ y) {
-  const uint64_t total = rows * extent;
+// dequantize_one with zero point 0 (quantization.rs:440-451).  One CTA per
+// row: the row's scale is read once, each thread turns 16 codes (one 16-byte
+// load) into four 16-byte streaming stores, several loads in flight.
+__global__ void __launch_bounds__(256) dequantize_i8_rows_kernel(const int8_t* __restrict__ codes,
+                                                                  const float* __restrict__ scales, uint64_t rows,
+                                                                  uint64_t extent, float* __restrict__ y) {
   const bool vec = (extent % 16 == 0) && ((uintptr_t)codes % 16 == 0) && ((uintptr_t)y % 16 == 0);
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+  const float s = __ldg(scales + row);
+  const int8_t* cr = codes + row * extent;
+  float* yr = y + row * extent;
+  auto dec = [s](uint32_t w, int j) {
+    const int8_t code = (int8_t)((w >> (8 * j)) & 0xff);
+    return code == 0 ? 0.0f : __fmul_rn((float)code, s);
+  };
   if (vec) {
-    const uint4* c16 = reinterpret_cast<const uint4*>(codes);
-    float4* y4 = reinterpret_cast<float4*>(y);
-    for (uint64_t v = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; v < total / 16; v += stride) {
-      const uint4 c = ld_global_nc_u4(c16 + v);
-      const float s = __ldg(scales + (v * 16) / extent);
-      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+    const uint4* c16 = reinterpret_cast<const uint4*>(cr);
+    float4* y4 = reinterpret_cast<float4*>(yr);
+    const uint32_t nv = (uint32_t)(extent / 16);
+    constexpr int U = 2;
+    for (uint32_t v0 = threadIdx.x; v0 < nv; v0 += blockDim.x * U) {
+      uint4 c[U];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float o[4];
+      for (int u = 0; u < U; ++u)
+        if (v0 + u * blockDim.x < nv) c[u] = ld_global_nc_u4(c16 + v0 + u * blockDim.x);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int8_t code = (int8_t)((w[q] >> (8 * j)) & 0xff);
-          o[j] = code == 0 ? 0.0f : __fmul_rn((float)code, s);
+      for (int u = 0; u < U; ++u) {
+        const uint32_t v = v0 + u * blockDim.x;
+        if (v < nv) {
+          const uint32_t w[4] = {c[u].x, c[u].y, c[u].z, c[u].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            st_global_stream(y4 + v * 4 + q, make_float4(dec(w[q], 0), dec(w[q], 1), dec(w[q], 2), dec(w[q], 3)));
         }
-        st_global_stream(y4 + v * 4 + q, make_float4(o[0], o[1], o[2], o[3]));
       }
     }
   } else {
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total; i += stride) {
-      const int8_t code = codes[i];
-      y[i] = code == 0 ? 0.0f : __fmul_rn((float)code, scales[i / extent]);
+    for (uint64_t i = threadIdx.x; i < extent; i += blockDim.x) {
+      const int8_t code = cr[i];
+      yr[i] = code == 0 ? 0.0f : __fmul_rn((float)code, s);
     }
+  }
   }
 }
 
 void launch_dequantize_i8_rows(const int8_t* codes, const float* scales, uint64_t rows, uint64_t extent, float* y,
                                int sm_count, cudaStream_t stream) {
   if (rows == 0 || extent == 0) return;
-  dequantize_i8_rows_kernel<<<(unsigned)(sm_count * 8), 256, 0, stream>>>(codes, scales, rows, extent, y);
+  const unsigned threads = (unsigned)umin64(256, std::max<uint64_t>(32, (extent / 16 + 31) / 32 * 32));
+  (void)sm_count;
+  const unsigned grid = (unsigned)rows;
+  dequantize_i8_rows_kernel<<<grid, threads, 0, stream>>>(codes, scales, rows, extent, y);
 }
 
 }  // namespace tc
