@@ -301,6 +301,23 @@ def family_suite(fam, torch, world, steps_small, warmup):
     gsteps = max(2, steps_small // 2)
     ms = time_device(lambda i: fam.gemm_bf16(ga, wt, "silu", out=cc, check=False), gsteps, warmup, world)
     rec("gemm_bf16_silu_8192x4096x14336", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps, tflops)
+    if world > 1:
+        # N-sharded contraction: each rank computes [8192, 14336/W] on its
+        # tensor cores, one NCCL all-gather assembles C (strong scaling; the
+        # whole-job FLOPs are the single contraction's)
+        from tiler_b200 import sharding
+        rank = torch.distributed.get_rank()
+        c0, c1 = sharding.row_range(14336, rank, world)
+        if (c1 - c0) % 256 == 0:
+            ws_ = wt[c0:c1].contiguous()
+            cl = torch.empty(8192, c1 - c0, device=dev, dtype=torch.bfloat16)
+            ms = time_device(lambda i: fam.gemm_bf16(ga, ws_, "silu", out=cl, check=False), gsteps, warmup, world)
+            rec("gemm_bf16_silu_nsharded_local", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps, tflops * world)
+            ms = time_device(lambda i: sharding.gemm_n_sharded(
+                ga, ws_, lambda a_, w_: fam.gemm_bf16(a_, w_, "silu", out=cl, check=False), assemble=False),
+                gsteps, warmup, world)
+            rec("gemm_bf16_silu_nsharded_allgather", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps,
+                tflops * world)
     del table, ga, wt, cc
     torch.cuda.empty_cache()
     return out

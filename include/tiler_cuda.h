@@ -160,6 +160,9 @@ int32_t tiler_cuda_sync(void* stream, uint64_t timeout_ns);
  * 3828-4040): the grouping this backend declares for [rows, count]. */
 int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, uint64_t count,
                                  tiler_cuda_grouping* out);
+/* The same proposal for a stated SM count, without a device (planning runs
+ * on a build host in the reference: session::compile, session.rs:2587). */
+int32_t tiler_cuda_plan_grouping_for(int32_t sm_count, uint64_t rows, uint64_t count, tiler_cuda_grouping* out);
 /* allocate_dispatch (adapter.rs:672-674): workspace bytes the grouped fold
  * needs (partials + per-row completion tickets). */
 uint64_t tiler_cuda_grouped_workspace_bytes(uint64_t rows, const tiler_cuda_grouping* g);

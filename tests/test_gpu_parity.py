@@ -390,3 +390,19 @@ def test_gemm_silu_epilogue_is_the_bf16_rounding_of_the_certified_silu(fam, orac
     want = want[0, :keep.size]
     bad = np.nonzero(got != want)[0]
     assert bad.size == 0, (bad[:5], keep[bad[:5]], got[bad[:5]], want[bad[:5]])
+
+
+def test_route_a_program_through_the_runtime_adapter(fam, oracle_lib):
+    from tiler_b200 import adapter as A
+    x = seeded_normal(40, 64 * 4096).reshape(64, 4096)
+    w = seeded_uniform(41, 4096, 0.5, 1.5)
+    ad = A.CudaRuntimeAdapter(device=torch.cuda.current_device())
+    payload = A.Payload("sm_100a", 32, (A.Entry("rms", "tiler_cuda.rms_norm_f32"),
+                                          A.Entry("sum", "tiler_cuda.sum_f32.grouped")))
+    out = A.route_with_adapter(payload, [A.Launch("rms", {"x": cuda(x), "w": cuda(w)}),
+                                         A.Launch("sum", {"x": cuda(x.reshape(-1))})], ad)
+    ad.close()
+    assert_bits_equal(host(out[0]), oracle_lib.rms_norm_f32(x, w)[1])
+    g = fam.plan_grouping(1, x.size)
+    assert_bits_equal(host(out[1]).reshape(1), oracle_lib.grid_fold(x.reshape(-1), g)[1])
+    assert ad.trace.index("commit") < ad.trace.index("dispatch")

@@ -82,6 +82,7 @@ SIGNATURES = {
     "tiler_cuda_status_decode": (i32, [C.POINTER(Status), C.POINTER(Error)]),
     "tiler_cuda_sync": (i32, [P, u64]),
     "tiler_cuda_plan_grouping": (i32, [P, u64, u64, C.POINTER(Grouping)]),
+    "tiler_cuda_plan_grouping_for": (i32, [i32, u64, u64, C.POINTER(Grouping)]),
     "tiler_cuda_grouped_workspace_bytes": (u64, [u64, C.POINTER(Grouping)]),
     "tiler_cuda_sum_f32": (i32, [P, P, P, u64, u64, C.POINTER(Grouping), P, u64, P]),
     "tiler_cuda_max_f32": (i32, [P, P, P, u64, u64, C.POINTER(Grouping), P, u64, P]),

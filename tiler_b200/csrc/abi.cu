@@ -282,16 +282,15 @@ int32_t tiler_cuda_sync(void* stream, uint64_t timeout_ns) {
 
 // ---- reductions --------------------------------------------------------------
 
-int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, uint64_t count,
-                                 tiler_cuda_grouping* out) {
-  if (!ctx || !out || count == 0) return TILER_CUDA_INVALID_APPLICATION;
+int32_t tiler_cuda_plan_grouping_for(int32_t sm_count, uint64_t rows, uint64_t count, tiler_cuda_grouping* out) {
+  if (sm_count <= 0 || !out || count == 0) return TILER_CUDA_INVALID_APPLICATION;
   const uint32_t T = 512, k = 4;
   const uint64_t per_round = (uint64_t)T * k;
   // Partitions: an exact divisor of count, aiming at 8 rounds per partition
   // and at least two CTAs per SM across all rows.
   const uint64_t target_per = per_round * 16;
   uint64_t want = std::max<uint64_t>(1, count / target_per);
-  const uint64_t min_ctas = 2ull * ctx->facts.sm_count;
+  const uint64_t min_ctas = 2ull * (uint64_t)sm_count;
   if (rows * want < min_ctas) want = std::max<uint64_t>(want, std::min<uint64_t>(count / per_round, (min_ctas + rows - 1) / rows));
   uint64_t best = 1;
   for (uint64_t d = std::max<uint64_t>(want, 1); d >= 1; --d)
@@ -314,6 +313,12 @@ int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, u
     out->combine_threads = out->combine_k = out->combine_rounds = 0;
   }
   return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, uint64_t count,
+                                 tiler_cuda_grouping* out) {
+  if (!ctx) return TILER_CUDA_INVALID_APPLICATION;
+  return tiler_cuda_plan_grouping_for(ctx->facts.sm_count, rows, count, out);
 }
 
 uint64_t tiler_cuda_grouped_workspace_bytes(uint64_t rows, const tiler_cuda_grouping* g) {

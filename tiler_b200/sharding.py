@@ -1,0 +1,72 @@
+"""One process per GPU: how the hot-path families spread over the GPUs of a node.
+
+The reference is single-device; these are the backend's multi-GPU
+realizations, each a declared, deterministic order (so results stay
+bit-identical to a single-GPU run of the same declared grouping):
+
+* row families (RMS norm, softmax, quantize/decode, gather, maps): rank r of
+  W owns the contiguous row block ``row_range(rows, r, W)``; no collective;
+* the sum: rank r folds its contiguous shard of the contributor sequence
+  under the shard's grid grouping, the W partials are all-gathered and folded
+  strictly in rank order (partition r = rank r: a strict_partitioned_sum over
+  W partitions whose partition folds are the shard groupings);
+* the contraction: W is split along N; rank r computes C[:, shard r] on its
+  tensor cores and one all-gather assembles C (rank-major column blocks).
+
+The collective is torch.distributed (NCCL on GPUs, gloo in the CPU tests).
+The local compute is injected so the host logic is testable without a GPU.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def row_range(rows: int, rank: int, world: int):
+    """Contiguous row block of `rank`: [rows*rank//world, rows*(rank+1)//world)."""
+    return rows * rank // world, rows * (rank + 1) // world
+
+
+def causal_row_offset(rows: int, rank: int, world: int) -> int:
+    """The global row index of the shard's first row: a softmax shard passes
+    it as ``row_offset`` so the causal mask keeps ``global_row mod period``."""
+    return row_range(rows, rank, world)[0]
+
+
+def _strict_fold(values: np.ndarray) -> np.float32:
+    """Strict left fold seeded at the first value (evaluate.rs:555-585), NaN
+    canonicalized."""
+    acc = np.float32(values[0])
+    with np.errstate(invalid="ignore", over="ignore"):
+        for v in values[1:]:
+            acc = np.float32(acc + np.float32(v))
+    if np.isnan(acc):
+        return np.array([0x7FC00000], np.uint32).view(np.float32)[0]
+    return acc
+
+
+def sum_across_ranks(shard: torch.Tensor, local_sum, group=None) -> np.float32:
+    """The multi-GPU sum: ``local_sum(shard)`` is this rank's partial (a
+    0-d or 1-element tensor); the partials are all-gathered and folded in
+    rank order.  Every rank returns the same bits."""
+    world = dist.get_world_size(group)
+    partial = local_sum(shard).reshape(1).to(torch.float32)
+    gathered = torch.empty(world, dtype=torch.float32, device=partial.device)
+    dist.all_gather_into_tensor(gathered, partial, group=group)
+    return _strict_fold(gathered.cpu().numpy())
+
+
+def gemm_n_sharded(a: torch.Tensor, w_shard: torch.Tensor, local_gemm, group=None, assemble: bool = True):
+    """C = local_gemm(a, w_shard) on every rank ([M, N/W] each), then one
+    all-gather.  Returns [M, N] (assemble=True) or the rank-major blocks
+    [W, M, N/W] as gathered."""
+    world = dist.get_world_size(group)
+    c_local = local_gemm(a, w_shard).contiguous()
+    m, n_local = c_local.shape
+    flat = torch.empty((world * m, n_local), dtype=c_local.dtype, device=c_local.device)
+    dist.all_gather_into_tensor(flat, c_local, group=group)
+    blocks = flat.view(world, m, n_local)
+    if not assemble:
+        return blocks
+    return blocks.permute(1, 0, 2).reshape(m, world * n_local)
