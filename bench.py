@@ -408,6 +408,55 @@ def run_tiler(args):
     return 0
 
 
+def run_profile_case(family: str, launches: int):
+    """A few launches of one family at its BASELINE config, for ncu captures
+    (profiles/*.txt name this command)."""
+    import torch
+
+    from tiler_b200 import families as fam
+    torch.cuda.set_device(0)
+    g = torch.Generator("cuda").manual_seed(3)
+    dev = "cuda"
+    if family in ("rms_f32", "rms_bf16"):
+        dt = torch.float32 if family == "rms_f32" else torch.bfloat16
+        x = torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=g).to(dt)
+        w = (torch.rand(RMS_EXTENT, device=dev, generator=g) + 0.5).to(dt)
+        y = torch.empty_like(x)
+        run = lambda: fam.rms_norm(x, w, out=y, check=False)
+    elif family == "softmax":
+        x = torch.randn(65536, 2048, device=dev, generator=g) * 3
+        y = torch.empty_like(x)
+        run = lambda: fam.softmax(x, causal_period=2048, out=y, check=False)
+    elif family == "sum":
+        x = torch.rand(1 << 24, device=dev, generator=g) * 2 - 1
+        gr = fam.plan_grouping(1, 1 << 24)
+        ws = fam.grouped_workspace(1, gr)
+        run = lambda: fam.sum_f32(x, gr, ws)
+    elif family in ("quantize", "dequantize"):
+        x = torch.randn(16384, 4096, device=dev, generator=g)
+        codes, scales = fam.quantize_i8_rows(x)
+        run = (lambda: fam.quantize_i8_rows(x, check=False)) if family == "quantize" else \
+            (lambda: fam.dequantize_i8_rows(codes, scales))
+    elif family == "gather":
+        table = (torch.randn(128256, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        ids = torch.randint(0, 128256, (8192,), device=dev, dtype=torch.int32, generator=g)
+        out = torch.empty(8192, 4096, device=dev, dtype=torch.bfloat16)
+        run = lambda: fam.gather_rows(table, ids, out=out, check=False)
+    elif family in ("gemm", "gemm_small"):
+        m = 8192 if family == "gemm" else 2048
+        a = (torch.randn(m, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w = (torch.randn(14336, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        c = torch.empty(m, 14336, device=dev, dtype=torch.bfloat16)
+        run = lambda: fam.gemm_bf16(a, w, "silu", out=c, check=False)
+    else:
+        raise SystemExit(f"unknown family {family}")
+    for _ in range(launches):
+        run()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": family, "launches": launches}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -417,7 +466,11 @@ def main():
     ap.add_argument("--family-steps", type=int, default=20)
     ap.add_argument("--no-families", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", default=None, help="launch one family's kernel a few times (for ncu)")
+    ap.add_argument("--launches", type=int, default=4)
     args = ap.parse_args()
+    if args.profile:
+        return run_profile_case(args.profile, args.launches)
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return run_reference(args)
