@@ -412,9 +412,9 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
                          uint64_t row_offset, float* __restrict__ y, uint32_t group, tiler_cuda_status* st) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   double* table = reinterpret_cast<double*>(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + 2048);
-  float* rcp = reinterpret_cast<float*>(smem_raw + 2048 + 16);
-  uint32_t* poisoned = reinterpret_cast<uint32_t*>(smem_raw + 2048 + 16 + 4 * kSmxMaxGroup);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + 2048);  // one per row buffer
+  float* rcp = reinterpret_cast<float*>(smem_raw + 2048 + 128);
+  uint32_t* poisoned = reinterpret_cast<uint32_t*>(smem_raw + 2048 + 192);
   float* bufs = reinterpret_cast<float*>(smem_raw + 2048 + 256);
   // warp 0 folds the denominators (the oldest warp, so the scheduler tends to
   // favour its dependent chain); warp w + 1 handles row w of each group.
@@ -433,10 +433,8 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
   const uint64_t drop = policy_evict_first();
 
   load_exp_table(table);
-  if (threadIdx.x == 0) {
-    mbar_init(full, 1);
-    fence_barrier_init();
-  }
+  if (threadIdx.x < kSmxMaxGroup) mbar_init(&full[threadIdx.x], 1);
+  fence_barrier_init();
   __syncthreads();
 #ifdef TILER_SMX_PROBE_SPAN
   const uint64_t span_t0 = global_ns();
@@ -445,19 +443,19 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
   for (uint64_t g = 0; g < ngroups; ++g) {
     const uint64_t row0 = group_row0(g);
     const uint32_t n = (uint32_t)umin64(G, rows - row0);
-    if (threadIdx.x == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive_expect_tx(full, n * row_bytes);
-      for (uint32_t r = 0; r < n; ++r)
-        bulk_g2s(bufs + (uint64_t)r * ext, x + (row0 + r) * extent, row_bytes, full, drop);
+    // each row warp loads its own row; its previous bulk store must have
+    // finished reading the buffer first
+    bool ok = true;
+    if (!chain_warp && warp < n) {
+      if (lane == 0) {
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        mbar_arrive_expect_tx(&full[warp], row_bytes);
+        bulk_g2s(bufs + (uint64_t)warp * ext, x + (row0 + warp) * extent, row_bytes, &full[warp], drop);
+      }
+      ok = mbar_wait(&full[warp], (uint32_t)(g & 1), st);
     }
 #ifdef TILER_SMX_PROBE_TIMES
-    long long t0 = clock64();
-#endif
-    const bool ok = mbar_wait(full, (uint32_t)(g & 1), st);
-    if (!__syncthreads_and(ok)) return;
-#ifdef TILER_SMX_PROBE_TIMES
-    long long t1 = clock64();
+    long long t0 = clock64(), t1 = t0;
 #endif
 
     if (!chain_warp && warp < n) {
@@ -506,7 +504,10 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
       for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (lane == 0) poisoned[warp] = bad;
     }
-    __syncthreads();
+    if (!__syncthreads_and(ok)) {
+      if (lane == 0 && !chain_warp) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      return;
+    }
 #ifdef TILER_SMX_PROBE_TIMES
     long long t2 = clock64();
 #endif
@@ -553,24 +554,33 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
 #endif
 
     if (!chain_warp && warp < n) {
-      // ---- out = e * r (softmax.rs:306-312) -----------------------------------
+      // ---- out = e * r (softmax.rs:306-312), written in place, then one bulk store
       const uint64_t row = row0 + warp;
       const float r = rcp[warp];
-      const float4* b4 = reinterpret_cast<const float4*>(bufs + (uint64_t)warp * ext);
-      float4* yr = reinterpret_cast<float4*>(y + row * extent);
+      float4* b4 = reinterpret_cast<float4*>(bufs + (uint64_t)warp * ext);
       if (is_nan_bits(r)) {
         const float nanv = __uint_as_float(kCanonicalNan);
-        for (uint32_t v = lane; v < ext / 4; v += 32) st_global_stream(yr + v, make_float4(nanv, nanv, nanv, nanv));
+        for (uint32_t v = lane; v < ext / 4; v += 32) b4[v] = make_float4(nanv, nanv, nanv, nanv);
       } else {
         // e is finite and >= 0 and r finite: the product is never NaN
         for (uint32_t v = lane; v < ext / 4; v += 32) {
           const float4 q = b4[v];
-          st_global_stream(yr + v, make_float4(__fmul_rn(q.x, r), __fmul_rn(q.y, r), __fmul_rn(q.z, r),
-                                               __fmul_rn(q.w, r)));
+          b4[v] = make_float4(__fmul_rn(q.x, r), __fmul_rn(q.y, r), __fmul_rn(q.z, r), __fmul_rn(q.w, r));
         }
       }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(y + row * extent),
+                     "r"(smem_u32(b4)), "r"(row_bytes)
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
     }
-    __syncthreads();  // the buffers are reloaded for the next group
+    // no barrier here: a row warp reloads only its own buffer, after its store
+#ifdef TILER_SMX_PROBE_TIMES
+    long long t4 = clock64();
+#endif
 #ifdef TILER_SMX_PROBE_SPAN
     if (threadIdx.x == 0 && g + 1 == ngroups) {
       uint64_t* T = reinterpret_cast<uint64_t*>(st) + 8;
@@ -580,13 +590,13 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
     }
 #endif
 #ifdef TILER_SMX_PROBE_TIMES
-    long long t4 = clock64();
     if (threadIdx.x == 0 && blockIdx.x == 100 && g < 8) {
       long long* T = reinterpret_cast<long long*>(st) + 8;  // probe scratch after the status word
       T[g * 4 + 0] = t1 - t0; T[g * 4 + 1] = t2 - t1; T[g * 4 + 2] = t3 - t2; T[g * 4 + 3] = t4 - t3;
     }
 #endif
   }
+  if (lane == 0 && !chain_warp) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete
 }
 
 __device__ __forceinline__ float masked_value(float v, uint64_t col, uint64_t diag, bool causal) {
