@@ -24,42 +24,62 @@ namespace tc {
 // p-1 has folded half of its first wave, so the pipelines' load, fold and
 // store phases interleave instead of hitting HBM and L2 all at once.
 //
-// One pipeline = 2 producer warps + 1 chain warp + kRmsNormWarps warps:
-//   producers  stream the wave's rows through a ring of shared-memory stages
-//              with 16-byte cp.async copies (completion on the stage's
-//              mbarrier); a stage is one 1 KB column slab of every row of the
-//              wave, rows padded by 16 bytes so the chain lanes' 16-byte reads
-//              down a column are bank-conflict-free;
+// One pipeline = 1 producer warp + 1 chain warp + kRmsNormWarps warps:
+//   producer   streams the wave's rows through a ring of shared-memory stages:
+//              per stage, lane r issues one bulk copy (cp.async.bulk) of row
+//              r's 2 KB column slab, completing on the stage's mbarrier; rows
+//              are padded by 16 bytes so the chain lanes' 16-byte reads down
+//              a column are bank-conflict-free.  (Bulk copies cost a roughly
+//              fixed time each, so slabs are 2 KB rather than 1 KB: 1 KB
+//              slabs halve the load rate; cp.async 16-byte copies, the
+//              alternative, put 64 threads' worth of issue next to the chain.)
 //   chain      lane r folds row r's squares strictly in column order
-//              (rms_norm.rs:147-170), loading 8 vectors ahead of the adds;
+//              (rms_norm.rs:147-170), the shared-memory loads of the next 8
+//              vectors issued before the adds of the current 8;
 //   normalize  once the wave's scales are known (mean = total/N, t = mean +
 //              eps, correctly rounded 1/sqrt(t)), re-read the wave's rows (an
 //              L2 hit, evict_first) and write y = w*(x*s) with streaming
-//              stores, while the producers and the chain move on.
+//              stores, while the producer and the chain move on.  A broadcast
+//              weight row is staged in shared memory once per CTA.
 
+#ifndef TILER_RMS_BULK_LOAD
+#define TILER_RMS_BULK_LOAD 1
+#endif
+// pipeline p > 0 starts once pipeline p - 1 has folded NUM/DEN of its first wave
+#ifndef TILER_RMS_STAGGER_NUM
+#define TILER_RMS_STAGGER_NUM 1
+#endif
+#ifndef TILER_RMS_STAGGER_DEN
+#define TILER_RMS_STAGGER_DEN 2
+#endif
 #ifndef TILER_RMS_WAVE
 #define TILER_RMS_WAVE 28
 #endif
 #ifndef TILER_RMS_STAGES
-#define TILER_RMS_STAGES 5
+#define TILER_RMS_STAGES 3
 #endif
 #ifndef TILER_RMS_PIPES
 #define TILER_RMS_PIPES 1
 #endif
 #ifndef TILER_RMS_NORM_WARPS
-#define TILER_RMS_NORM_WARPS 10
+#define TILER_RMS_NORM_WARPS 14
 #endif
 #ifndef TILER_RMS_SLAB
-#define TILER_RMS_SLAB 1024
+#define TILER_RMS_SLAB 2048
 #endif
 constexpr int kRmsSlabBytes = TILER_RMS_SLAB;
 constexpr int kRmsPitch = kRmsSlabBytes + 16;
 constexpr int kRmsWave = TILER_RMS_WAVE;  // rows per wave (one chain lane per row), <= 32
 constexpr int kRmsStages = TILER_RMS_STAGES;
 constexpr int kRmsPipes = TILER_RMS_PIPES;
-constexpr int kRmsLoadWarps = 2;
+constexpr int kRmsLoadWarps = TILER_RMS_BULK_LOAD ? 1 : 2;
 constexpr int kRmsNormWarps = TILER_RMS_NORM_WARPS;
 constexpr int kRmsPipeWarps = kRmsLoadWarps + 1 + kRmsNormWarps;
+// x is loaded with evict_last so it stays in L2 until the normalize pass
+// re-reads it (with evict_first).
+#ifndef TILER_RMS_KEEP_X
+#define TILER_RMS_KEEP_X 1
+#endif
 constexpr int kRmsThreads = 32 * kRmsPipeWarps * kRmsPipes;
 
 struct RmsPipeSmem {
@@ -71,14 +91,24 @@ struct RmsPipeSmem {
   uint64_t started;  // arrived once this pipeline has folded half of its first wave
   float scale[2][kRmsWave];
 };
+// The broadcast weight row is staged once per CTA when it fits.
+constexpr int kRmsWeightBytes = 16384;
+#ifndef TILER_RMS_NORM_U
+#define TILER_RMS_NORM_U 8
+#endif
 struct RmsSmem {
   RmsPipeSmem pipe[kRmsPipes];
+  alignas(16) uint8_t wrow[kRmsWeightBytes];
   int abort;
 };
 constexpr size_t kRmsSmemBytes = sizeof(RmsSmem);
 
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async16_hint(uint32_t saddr, const void* g, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(saddr), "l"(g), "l"(policy)
+               : "memory");
 }
 __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -133,20 +163,35 @@ __device__ __forceinline__ uint4 ld_u4_policy(const void* p, uint64_t policy) {
 }
 
 // Folds `n` 16-byte vectors of one staged row into acc (strict order).
+// Software-pipelined: the shared-memory loads of batch k + 1 are issued
+// before the adds of batch k, so the dependent add chain never waits on a
+// load's latency (the warp issues in order).
+template <class E>
+__device__ __forceinline__ void rms_fold_batch(float& acc, const uint4 (&q)[8]) {
+#pragma unroll
+  for (uint32_t b = 0; b < 8; ++b) {
+    float e[E::kPerVec];
+    E::unpack(q[b], e);
+#pragma unroll
+    for (int j = 0; j < E::kPerVec; ++j) acc = __fadd_rn(acc, __fmul_rn(e[j], e[j]));
+  }
+}
 template <class E>
 __device__ __forceinline__ float rms_fold_vectors(float acc, uint32_t rowp, uint32_t v, uint32_t n) {
   constexpr uint32_t B = 8;
-  for (; v + B <= n; v += B) {
-    uint4 q[B];
+  if (v + B <= n) {
+    uint4 q[B], qn[B];
 #pragma unroll
     for (uint32_t b = 0; b < B; ++b) q[b] = lds_u4_nv(rowp + (v + b) * 16);
+    v += B;
+    for (; v + B <= n; v += B) {
 #pragma unroll
-    for (uint32_t b = 0; b < B; ++b) {
-      float e[E::kPerVec];
-      E::unpack(q[b], e);
+      for (uint32_t b = 0; b < B; ++b) qn[b] = lds_u4_nv(rowp + (v + b) * 16);
+      rms_fold_batch<E>(acc, q);
 #pragma unroll
-      for (int j = 0; j < E::kPerVec; ++j) acc = __fadd_rn(acc, __fmul_rn(e[j], e[j]));
+      for (uint32_t b = 0; b < B; ++b) q[b] = qn[b];
     }
+    rms_fold_batch<E>(acc, q);
   }
   for (; v < n; ++v) {
     float e[E::kPerVec];
@@ -184,22 +229,50 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
   if (threadIdx.x == 0) {
     for (int p = 0; p < kRmsPipes; ++p) {
       RmsPipeSmem& Q = SS.pipe[p];
-      for (int s = 0; s < kRmsStages; ++s) { mbar_init(&Q.full[s], kRmsLoadWarps * 32); mbar_init(&Q.empty[s], 1); }
+      for (int s = 0; s < kRmsStages; ++s) { mbar_init(&Q.full[s], TILER_RMS_BULK_LOAD ? 1 : kRmsLoadWarps * 32); mbar_init(&Q.empty[s], 1); }
       for (int s = 0; s < 2; ++s) { mbar_init(&Q.scale_full[s], 1); mbar_init(&Q.scale_empty[s], kRmsNormWarps); }
       mbar_init(&Q.started, 1);
     }
     SS.abort = 0;
     fence_barrier_init();
   }
+  const bool w_staged = w_row_stride == 0 && row_bytes <= (uint64_t)kRmsWeightBytes;
+  if (w_staged)
+    for (uint32_t i = threadIdx.x; i < row_bytes / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(SS.wrow)[i] = __ldg(reinterpret_cast<const uint4*>(w) + i);
   __syncthreads();
   volatile int* abort_flag = &SS.abort;
   if (nwaves == 0) return;
+#ifdef TILER_RMS_PROBE_TL
+  unsigned long long* tl = reinterpret_cast<unsigned long long*>(st) + 64 + blockIdx.x * 8;
+  if (threadIdx.x == 0) tl[0] = global_ns();
+#endif
 
   if (pwarp < kRmsLoadWarps) {
     // ---- producers -----------------------------------------------------------
-    const uint32_t t = threadIdx.x % (32 * kRmsPipeWarps);
+    const uint32_t t = pwarp * 32 + lane;
+    // x stays in L2 until the normalize pass re-reads it (with evict_first)
+    const uint64_t keep = TILER_RMS_KEEP_X ? policy_evict_last() : policy_evict_normal();
     if (pipe > 0 && !mbar_wait(&SS.pipe[pipe - 1].started, 0, st))
       *abort_flag = 1;
+#if TILER_RMS_BULK_LOAD
+    // one warp: per stage, lane r issues one bulk copy of row r's slab
+    // (padded pitch), completing on the stage's mbarrier
+    if (pwarp == 0) {
+      for (uint64_t i = 0; i < total && !*abort_flag; ++i) {
+        const uint32_t stage = i % kRmsStages;
+        const uint64_t use = i / kRmsStages;
+        if (use > 0 && !mbar_wait(&S.empty[stage], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
+        const uint64_t wv = i / nslabs, c = i % nslabs;
+        const uint32_t wr = wave_rows_of(wv);
+        const uint32_t bytes = (uint32_t)umin64(kRmsSlabBytes, row_bytes - c * kRmsSlabBytes);
+        const uint8_t* gbase = x + (rb + wave_first_row(wv)) * row_bytes + c * kRmsSlabBytes;
+        if (lane == 0) mbar_arrive_expect_tx(&S.full[stage], bytes * wr);
+        __syncwarp();
+        if (lane < wr) bulk_g2s(&S.stage[stage][lane * kRmsPitch], gbase + lane * row_bytes, bytes, &S.full[stage], keep);
+      }
+    }
+#else
     for (uint64_t i = 0; i < total && !*abort_flag; ++i) {
       const uint32_t stage = i % kRmsStages;
       const uint64_t use = i / kRmsStages;
@@ -211,11 +284,19 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
       const uint8_t* gbase = x + (rb + wave_first_row(wv)) * row_bytes + c * kRmsSlabBytes;
       for (uint32_t q = t; q < wr * (kRmsSlabBytes / 16); q += kRmsLoadWarps * 32) {
         const uint32_t r = q / (kRmsSlabBytes / 16), c16 = q % (kRmsSlabBytes / 16);
+#if TILER_RMS_KEEP_X
+        if (c16 < chunks) cp_async16_hint(sbase + r * kRmsPitch + c16 * 16, gbase + r * row_bytes + c16 * 16, keep);
+#else
         if (c16 < chunks) cp_async16(sbase + r * kRmsPitch + c16 * 16, gbase + r * row_bytes + c16 * 16);
+#endif
       }
       cp_async_arrive(&S.full[stage]);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
+#endif
+#ifdef TILER_RMS_PROBE_TL
+    if (threadIdx.x == 0) tl[5] = global_ns();
+#endif
   } else if (pwarp == kRmsLoadWarps) {
     // ---- chain warp ------------------------------------------------------------
     bool signalled = false;
@@ -246,7 +327,7 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&S.empty[stage]);
-          if (!signalled && (c + 1) * 2 >= nslabs) { mbar_arrive(&S.started); signalled = true; }
+          if (!signalled && (c + 1) * TILER_RMS_STAGGER_DEN >= nslabs * TILER_RMS_STAGGER_NUM) { mbar_arrive(&S.started); signalled = true; }
         }
       }
       if (*abort_flag) break;
@@ -257,6 +338,9 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
       const uint64_t use = wv >> 1;
       if (use > 0 && !mbar_wait(&S.scale_empty[slot], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
       if (lane < wr) S.scale[slot][lane] = s;
+#ifdef TILER_RMS_PROBE_TL
+      if (lane == 0 && wv < 2) tl[1 + wv] = global_ns();
+#endif
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.scale_full[slot]);
     }
@@ -277,24 +361,23 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
         const uint8_t* xr = x + row * row_bytes;
         const uint8_t* wrow = w + (int64_t)row * w_row_stride * (int64_t)esize;
         uint8_t* yr = y + row * row_bytes;
-        constexpr int U = 8;  // 16-byte loads in flight per lane
+        constexpr int U = TILER_RMS_NORM_U;  // 16-byte loads of x in flight per lane
         for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * U) {
-          uint4 xv[U], wvv[U];
+          uint4 xv[U];
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const uint64_t v = v0 + 32 * u;
-            if (v < nvec) {
-              xv[u] = ld_u4_policy(xr + v * 16, drop);
-              wvv[u] = __ldg(reinterpret_cast<const uint4*>(wrow + v * 16));
-            }
+            if (v < nvec) xv[u] = ld_u4_policy(xr + v * 16, drop);
           }
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const uint64_t v = v0 + 32 * u;
             if (v < nvec) {
+              const uint4 wq = w_staged ? reinterpret_cast<const uint4*>(SS.wrow)[v]
+                                        : __ldg(reinterpret_cast<const uint4*>(wrow + v * 16));
               float xe[E::kPerVec], we[E::kPerVec], ye[E::kPerVec];
               E::unpack(xv[u], xe);
-              E::unpack(wvv[u], we);
+              E::unpack(wq, we);
 #pragma unroll
               for (int j = 0; j < E::kPerVec; ++j) ye[j] = canon(__fmul_rn(we[j], __fmul_rn(xe[j], s)));
               st_global_stream_u4(reinterpret_cast<uint4*>(yr + v * 16), E::pack(ye));
@@ -304,6 +387,9 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
       }
 #endif
       __syncwarp();
+#ifdef TILER_RMS_PROBE_TL
+      if (lane == 0 && wv < 2) atomicMax(&tl[3 + wv], global_ns());
+#endif
       if (lane == 0) mbar_arrive(&S.scale_empty[slot]);
     }
   }
