@@ -282,7 +282,8 @@ def family_suite(fam, torch, world, steps_small, warmup):
     cd = torch.empty_like(codes)
 
     def run_dec(i):
-        L.tiler_cuda_dequantize_i8_rows(ctx, stream, codes.data_ptr(), scales.data_ptr(), 16384, 4096, yq.data_ptr())
+        L.tiler_cuda_dequantize_i8_rows(ctx, stream, None, codes.data_ptr(), scales.data_ptr(), 16384, 4096,
+                                        yq.data_ptr())
     ms = time_device(run_dec, steps_small, warmup, world)
     rec("dequantize_i8_16384x4096", "GB/s", qbytes, ms, steps_small, hbm)
     del xq, yq, codes, cd
@@ -436,7 +437,7 @@ def run_profile_case(family: str, launches: int):
         x = torch.randn(16384, 4096, device=dev, generator=g)
         codes, scales = fam.quantize_i8_rows(x)
         run = (lambda: fam.quantize_i8_rows(x, check=False)) if family == "quantize" else \
-            (lambda: fam.dequantize_i8_rows(codes, scales))
+            (lambda: fam.dequantize_i8_rows(codes, scales, check=False))
     elif family == "gather":
         table = (torch.randn(128256, 4096, device=dev, generator=g) * 0.02).to(torch.bfloat16)
         ids = torch.randint(0, 128256, (8192,), device=dev, dtype=torch.int32, generator=g)

@@ -226,9 +226,12 @@ int32_t tiler_cuda_softmax_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda
 int32_t tiler_cuda_quantize_i8_rows(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
                                     const float* x, uint64_t rows, uint64_t extent, int8_t* codes,
                                     float* scales);
-/* dequantize_one (quantization.rs:440-451) with zero point 0, per-row scale. */
-int32_t tiler_cuda_dequantize_i8_rows(tiler_cuda_context* ctx, void* stream, const int8_t* codes,
-                                      const float* scales, uint64_t rows, uint64_t extent, float* y);
+/* dequantize_one (quantization.rs:440-451) with zero point 0, per-row scale.
+ * Decoding cannot fail on any input; `status` (nullable) only counts bounded
+ * waits of the staged kernel that ran out (TILER_CUDA_TIMEOUT). */
+int32_t tiler_cuda_dequantize_i8_rows(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                      const int8_t* codes, const float* scales, uint64_t rows,
+                                      uint64_t extent, float* y);
 /* The reference's own per-tensor unsigned family (U4: maximum 15, U8: 255). */
 int32_t tiler_cuda_quantize_affine_u8(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
                                       const float* x, uint64_t n, uint32_t scale_bits,

@@ -319,6 +319,26 @@ def test_quantize_refusals(fam):
     assert e.value.code == 9 and e.value.position == 0
 
 
+def test_quantize_staged_rows_refusals_and_extremes(fam, oracle_lib):
+    # 4096-wide rows take the shared-memory staged kernel: the first NaN of
+    # the earliest refused row is reported, and extreme magnitudes (largest
+    # finite, smallest subnormal) code like the oracle
+    x = seeded_normal(4, 4 * 4096).reshape(4, 4096)
+    x[0, 17] = np.float32(3.4028235e38)
+    x[1, 5] = np.float32(1e-45)
+    codes, scales = fam.quantize_i8_rows(cuda(x))
+    st, wc, ws, _ = oracle_lib.quantize_i8_rows(x)
+    assert st == 0 and (host(codes) == wc).all()
+    assert_bits_equal(host(scales), ws)
+    bad = x.copy()
+    bad[2, 3000] = np.nan
+    bad[2, 3500] = np.nan
+    bad[3, 10] = np.inf
+    with pytest.raises(fam.TilerCudaError) as e:
+        fam.quantize_i8_rows(cuda(bad))
+    assert e.value.code == 4 and e.value.position == 2 * 4096 + 3000
+
+
 def test_gather_full_config_is_bit_exact(fam):
     gen = torch.Generator("cuda").manual_seed(3)
     table = (torch.randn(128256, 4096, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)

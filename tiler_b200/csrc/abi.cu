@@ -449,12 +449,13 @@ int32_t tiler_cuda_quantize_i8_rows(tiler_cuda_context* ctx, void* stream, tiler
   return last_error_status();
 }
 
-int32_t tiler_cuda_dequantize_i8_rows(tiler_cuda_context* ctx, void* stream, const int8_t* codes,
-                                      const float* scales, uint64_t rows, uint64_t extent, float* y) {
+int32_t tiler_cuda_dequantize_i8_rows(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                      const int8_t* codes, const float* scales, uint64_t rows,
+                                      uint64_t extent, float* y) {
   CHECK_CTX(ctx);
   if (rows == 0 || extent == 0) return TILER_CUDA_OK;
   if (!codes || !scales || !y || rows > 0x7fffffffull) return TILER_CUDA_INVALID_APPLICATION;
-  launch_dequantize_i8_rows(codes, scales, rows, extent, y, ctx->facts.sm_count, S(stream));
+  launch_dequantize_i8_rows(codes, scales, rows, extent, y, ctx->facts.sm_count, S(stream), status);
   return last_error_status();
 }
 

@@ -33,7 +33,7 @@ int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t caus
 void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
                              tiler_cuda_status* st, int sm_count, cudaStream_t stream);
 void launch_dequantize_i8_rows(const int8_t* codes, const float* scales, uint64_t rows, uint64_t extent, float* y,
-                               int sm_count, cudaStream_t stream);
+                               int sm_count, cudaStream_t stream, tiler_cuda_status* st);
 
 // maps.cu
 void launch_silu(const float* x, uint64_t n, float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream);

@@ -769,6 +769,20 @@ __device__ __forceinline__ int8_t code_of(float xv, float scale, float inv) {
   return (int8_t)__float2int_rn(q);
 }
 
+// code_of for |x| <= max|x| of a NaN-free row: then |x * (1/scale)| stays
+// below 127 * (1 + 2^-21), so its rounding to an integer needs no clamp and
+// the value is finite.  The product is taken unless it lies within 2.5e-5 of
+// a half-integer; there the exact IEEE quotient decides (as in code_of).
+__device__ __forceinline__ int code_of_bounded(float xv, float scale, float inv) {
+  float q = __fmul_rn(xv, inv);
+  float r = rintf(q);
+  if (fabsf(__fsub_rn(q, r)) > 0.49997f) {
+    q = __fdiv_rn(xv, scale);
+    r = rintf(q);
+  }
+  return max(-127, min(127, __float2int_rn(r)));
+}
+
 // Row values are held in registers (up to kQMaxVec float4 per thread, rows of
 // up to 4096 f32 with 256 threads), so x is read from HBM exactly once: all
 // of a thread's loads are issued before the maximum consumes them.
@@ -868,17 +882,130 @@ __global__ void __launch_bounds__(kQThreads) quantize_i8_rows_kernel(const float
   }
 }
 
+// Staged variant for rows of up to 16 KB (16-byte aligned, extent a multiple
+// of 4): a persistent CTA double-buffers rows in shared memory, thread 0
+// bringing row i + 2 * grid in with one bulk copy while the CTA codes row i,
+// so every SM keeps 2 rows per CTA in flight at no register cost.  Same
+// numerics and error rules as the kernel above.
+constexpr int kQbThreads = 256;
+constexpr int kQbCtasPerSm = 6;
+constexpr uint32_t kQbMaxRowBytes = 16384;
+
+__global__ void __launch_bounds__(kQbThreads, kQbCtasPerSm)
+    quantize_i8_rows_bulk_kernel(const float* __restrict__ x, uint64_t rows, uint64_t extent,
+                                 int8_t* __restrict__ codes, float* __restrict__ scales, tiler_cuda_status* st) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  float* buf = reinterpret_cast<float*>(smem_raw);  // [2][kQbMaxRowBytes / 4]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + 2 * kQbMaxRowBytes);
+  __shared__ uint32_t nan_at[kQbThreads / 32];
+  __shared__ int abort_flag;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t row_bytes = (uint32_t)extent * 4, nvec = (uint32_t)(extent / 4);
+  const uint64_t pol = policy_evict_first();
+  auto issue = [&](uint64_t row, uint32_t b) {
+    mbar_arrive_expect_tx(&full[b], row_bytes);
+    bulk_g2s(buf + b * (kQbMaxRowBytes / 4), x + row * extent, row_bytes, &full[b], pol);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    if (blockIdx.x < rows) issue(blockIdx.x, 0);
+    if (blockIdx.x + gridDim.x < rows) issue(blockIdx.x + gridDim.x, 1);
+  }
+  __syncthreads();
+  uint32_t it = 0;
+  for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+    const uint32_t b = it & 1;
+    if (!mbar_wait(&full[b], (it >> 1) & 1, st)) abort_flag = 1;
+    const float4* b4 = reinterpret_cast<const float4*>(buf + b * (kQbMaxRowBytes / 4));
+    // max|x| as an unsigned maximum of the magnitude bits: for non-NaN
+    // values it orders like the float maximum (all magnitudes are >= +0);
+    // a NaN shows as a maximum above 0x7f800000 and is then located exactly.
+    uint32_t mb = 0;
+    for (uint32_t v = threadIdx.x; v < nvec; v += kQbThreads) {
+      const uint4 q = *reinterpret_cast<const uint4*>(b4 + v);
+      mb = max(mb, max(max(q.x & 0x7fffffffu, q.y & 0x7fffffffu), max(q.z & 0x7fffffffu, q.w & 0x7fffffffu)));
+    }
+    mb = __reduce_max_sync(0xffffffffu, mb);
+    if (lane == 0) nan_at[warp] = mb;
+    __syncthreads();
+    if (abort_flag) break;
+    mb = nan_at[0];
+    for (int i = 1; i < kQbThreads / 32; ++i) mb = max(mb, nan_at[i]);
+    if (mb > 0x7f800000u) {
+      // rare: the row holds a NaN; report its first column
+      uint32_t first_nan = 0xffffffffu;
+      for (uint32_t v = threadIdx.x; v < nvec; v += kQbThreads) {
+        const float4 q = b4[v];
+        const float e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (is_nan_bits(e[j])) first_nan = min(first_nan, v * 4 + j);
+      }
+      first_nan = __reduce_min_sync(0xffffffffu, first_nan);
+      __syncthreads();  // everyone has read nan_at
+      if (lane == 0) nan_at[warp] = first_nan;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int i = 1; i < kQbThreads / 32; ++i) first_nan = min(first_nan, nan_at[i]);
+        first_nan = min(first_nan, nan_at[0]);
+        report_error(st, row * extent + first_nan, TILER_CUDA_NAN_INPUT);
+      }
+    } else {
+      const float m = __uint_as_float(mb);
+      const float scale = __fdiv_rn(m, 127.0f);
+      if (threadIdx.x == 0) scales[row] = scale;
+      if (!is_positive_normal(scale)) {
+        if (threadIdx.x == 0) report_error(st, row * extent, TILER_CUDA_SCALE_DOMAIN);
+      } else {
+        const float inv = __frcp_rn(scale);
+        int* c4 = reinterpret_cast<int*>(codes + row * extent);
+        for (uint32_t v = threadIdx.x; v < nvec; v += kQbThreads) {
+          const float4 q = b4[v];
+          const float e[4] = {q.x, q.y, q.z, q.w};
+          int c[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) c[j] = code_of_bounded(e[j], scale, inv);
+          // cvt.pack d, a, b, c: d = c << 16 | sat8(a) << 8 | sat8(b)
+          uint32_t hi, packed;
+          asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(c[3]), "r"(c[2]));
+          asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(packed) : "r"(c[1]), "r"(c[0]), "r"(hi));
+          __stcs(c4 + v, (int)packed);
+        }
+      }
+    }
+    __syncthreads();  // buffer b and the reduction slots are free again
+    if (threadIdx.x == 0 && row + 2 * (uint64_t)gridDim.x < rows) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(row + 2 * (uint64_t)gridDim.x, b);
+    }
+  }
+  // a copy still in flight (abort) must land before the CTA's shared memory is released
+  if (threadIdx.x == 0 && abort_flag) {
+    for (uint32_t k = 0; k < 2; ++k) (void)mbar_wait(&full[(it + k) & 1], ((it + k) >> 1) & 1, nullptr);
+  }
+}
+
 void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
                              tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
   if (rows == 0) return;
-  (void)sm_count;  // one CTA per row measured fastest (short-lived CTAs keep many rows' loads in flight)
+  const bool staged = extent > 0 && extent % 4 == 0 && extent * 4 <= kQbMaxRowBytes && (uintptr_t)x % 16 == 0 &&
+                      (uintptr_t)codes % 4 == 0;
+  if (staged) {
+    const size_t smem = 2 * kQbMaxRowBytes + 16;
+    cudaFuncSetAttribute(quantize_i8_rows_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(quantize_i8_rows_bulk_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    const unsigned grid = (unsigned)umin64(rows, (uint64_t)sm_count * kQbCtasPerSm);
+    quantize_i8_rows_bulk_kernel<<<grid, kQbThreads, smem, stream>>>(x, rows, extent, codes, scales, st);
+    return;
+  }
+  // one CTA per row measured fastest here (short-lived CTAs keep many rows' loads in flight)
   const unsigned grid = (unsigned)rows;
   quantize_i8_rows_kernel<<<grid, kQThreads, 0, stream>>>(x, rows, extent, codes, scales, st);
 }
 
-// dequantize_one with zero point 0 (quantization.rs:440-451).  One CTA per
-// row: the row's scale is read once, each thread turns 16 codes (one 16-byte
-// load) into four 16-byte streaming stores, several loads in flight.
 __global__ void __launch_bounds__(256) dequantize_i8_rows_kernel(const int8_t* __restrict__ codes,
                                                                   const float* __restrict__ scales, uint64_t rows,
                                                                   uint64_t extent, float* __restrict__ y) {
@@ -921,11 +1048,93 @@ __global__ void __launch_bounds__(256) dequantize_i8_rows_kernel(const int8_t* _
   }
 }
 
+// Staged decode for rows whose codes and output are 16-byte aligned, extent
+// a multiple of 16 and at most 4096: a persistent CTA double-buffers a row's
+// codes (one bulk load), decodes them into a shared-memory output row and
+// writes it back with one bulk store, so the 4x larger output stream goes
+// through the copy engine instead of per-thread stores.
+constexpr int kDqThreads = 256;
+constexpr int kDqCtasPerSm = 4;
+constexpr uint32_t kDqMaxExtent = 4096;
+
+__global__ void __launch_bounds__(kDqThreads, kDqCtasPerSm)
+    dequantize_i8_rows_bulk_kernel(const int8_t* __restrict__ codes, const float* __restrict__ scales, uint64_t rows,
+                                   uint64_t extent, float* __restrict__ y, tiler_cuda_status* st) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  float* out = reinterpret_cast<float*>(smem_raw);                          // [2][kDqMaxExtent]
+  uint8_t* in = smem_raw + 2 * kDqMaxExtent * 4;                           // [2][kDqMaxExtent]
+  uint64_t* full = reinterpret_cast<uint64_t*>(in + 2 * kDqMaxExtent);     // [2]
+  __shared__ int abort_flag;
+  const uint32_t ext = (uint32_t)extent, nw = ext / 4;
+  const uint64_t pol = policy_evict_first();
+  auto issue = [&](uint64_t row, uint32_t b) {
+    mbar_arrive_expect_tx(&full[b], ext);
+    bulk_g2s(in + b * kDqMaxExtent, codes + row * extent, ext, &full[b], pol);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    if (blockIdx.x < rows) issue(blockIdx.x, 0);
+    if (blockIdx.x + gridDim.x < rows) issue(blockIdx.x + gridDim.x, 1);
+  }
+  __syncthreads();
+  uint32_t it = 0;
+  for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+    const uint32_t b = it & 1;
+    if (threadIdx.x == 0) {
+      // the store that last read out[b] (two rows ago) has finished reading
+      asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    }
+    if (!mbar_wait(&full[b], (it >> 1) & 1, st)) abort_flag = 1;
+    __syncthreads();
+    if (abort_flag) break;
+    const float s = __ldg(scales + row);
+    const uint32_t* c32 = reinterpret_cast<const uint32_t*>(in + b * kDqMaxExtent);
+    float4* o4 = reinterpret_cast<float4*>(out + b * kDqMaxExtent);
+    for (uint32_t v = threadIdx.x; v < nw; v += kDqThreads) {
+      const uint32_t w = c32[v];
+      float d[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int8_t code = (int8_t)((w >> (8 * j)) & 0xff);
+        d[j] = code == 0 ? 0.0f : __fmul_rn((float)code, s);
+      }
+      o4[v] = make_float4(d[0], d[1], d[2], d[3]);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(y + row * extent),
+                   "r"(smem_u32(out + b * kDqMaxExtent)), "r"(ext * 4)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      if (row + 2 * (uint64_t)gridDim.x < rows) issue(row + 2 * (uint64_t)gridDim.x, b);
+    }
+  }
+  if (threadIdx.x == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    // a load still in flight (abort) must land before shared memory is released
+    if (abort_flag)
+      for (uint32_t k = 0; k < 2; ++k) (void)mbar_wait(&full[(it + k) & 1], ((it + k) >> 1) & 1, nullptr);
+  }
+}
+
 void launch_dequantize_i8_rows(const int8_t* codes, const float* scales, uint64_t rows, uint64_t extent, float* y,
-                               int sm_count, cudaStream_t stream) {
+                               int sm_count, cudaStream_t stream, tiler_cuda_status* st) {
   if (rows == 0 || extent == 0) return;
+  const bool staged = extent % 16 == 0 && extent <= kDqMaxExtent && (uintptr_t)codes % 16 == 0 &&
+                      (uintptr_t)y % 16 == 0;
+  if (staged) {
+    const size_t smem = 2 * kDqMaxExtent * 5 + 16;
+    cudaFuncSetAttribute(dequantize_i8_rows_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(dequantize_i8_rows_bulk_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    const unsigned grid = (unsigned)umin64(rows, (uint64_t)sm_count * kDqCtasPerSm);
+    dequantize_i8_rows_bulk_kernel<<<grid, kDqThreads, smem, stream>>>(codes, scales, rows, extent, y, st);
+    return;
+  }
   const unsigned threads = (unsigned)umin64(256, std::max<uint64_t>(32, (extent / 16 + 31) / 32 * 32));
-  (void)sm_count;
   const unsigned grid = (unsigned)rows;
   dequantize_i8_rows_kernel<<<grid, threads, 0, stream>>>(codes, scales, rows, extent, y);
 }

@@ -255,13 +255,16 @@ def quantize_i8_rows(x: torch.Tensor, check=True):
     return codes, scales
 
 
-def dequantize_i8_rows(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+def dequantize_i8_rows(codes: torch.Tensor, scales: torch.Tensor, check=True) -> torch.Tensor:
     """dequantize_one with zero point 0 (quantization.rs:440-451)."""
     extent = codes.shape[-1]
     rows = codes.numel() // extent
     y = torch.empty(codes.shape, dtype=torch.float32, device=codes.device)
-    _check(N.lib().tiler_cuda_dequantize_i8_rows(context(), _stream(), _ptr(codes), _ptr(scales), rows, extent,
-                                                 _ptr(y)), "dequantize_i8_rows")
+    st = _status() if check else None
+    _check(N.lib().tiler_cuda_dequantize_i8_rows(context(), _stream(), st.ptr if st else 0, _ptr(codes),
+                                                 _ptr(scales), rows, extent, _ptr(y)), "dequantize_i8_rows")
+    if st:
+        _raise_from(st, "dequantize_i8_rows")
     return y
 
 
