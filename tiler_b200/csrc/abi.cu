@@ -87,7 +87,8 @@ int32_t validate_grouping(uint64_t rows, uint64_t count, const tiler_cuda_groupi
   if (rows * g->partitions > 0x7fffffffull) return TILER_CUDA_SHAPE_TOO_LARGE;
   if (g->partitions > 1) {
     if (!workspace) return TILER_CUDA_INVALID_APPLICATION;
-    if (workspace_bytes < tiler_cuda_grouped_workspace_bytes(rows, g)) return TILER_CUDA_WORKSPACE_TOO_SMALL;
+    const uint64_t partial_bytes = (rows * g->partitions * 4 + 255) / 256 * 256;
+    if (workspace_bytes < partial_bytes + rows * 4) return TILER_CUDA_WORKSPACE_TOO_SMALL;
     if ((uintptr_t)workspace % 16) return TILER_CUDA_INVALID_APPLICATION;
   }
   return TILER_CUDA_OK;
@@ -321,10 +322,19 @@ int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, u
   return tiler_cuda_plan_grouping_for(ctx->facts.sm_count, rows, count, out);
 }
 
+// Workspace layout: partials [rows * P] | tickets [rows] | round totals
+// [rows * P * rounds].  The first two regions are required; the third
+// (reported by tiler_cuda_grouped_workspace_bytes) enables the
+// round-parallel kernel, and a workspace without it takes the
+// CTA-per-partition kernel with the same results.
+static uint64_t grouped_base_bytes(uint64_t rows, const tiler_cuda_grouping* g) {
+  const uint64_t partial_bytes = (rows * g->partitions * 4 + 255) / 256 * 256;
+  return partial_bytes + (rows * 4 + 255) / 256 * 256;
+}
+
 uint64_t tiler_cuda_grouped_workspace_bytes(uint64_t rows, const tiler_cuda_grouping* g) {
   if (!g || g->partitions <= 1) return 0;
-  const uint64_t partial_bytes = (rows * g->partitions * 4 + 255) / 256 * 256;
-  return partial_bytes + rows * 4;
+  return grouped_base_bytes(rows, g) + rows * g->partitions * (uint64_t)g->rounds * 4;
 }
 
 static int32_t grouped(int op, tiler_cuda_context* ctx, void* stream, const float* x, uint64_t rows, uint64_t count,
@@ -343,7 +353,10 @@ static int32_t grouped(int op, tiler_cuda_context* ctx, void* stream, const floa
   float* partials = (float*)ws;
   unsigned int* tickets =
       ws ? (unsigned int*)((uint8_t*)ws + (rows * g->partitions * 4 + 255) / 256 * 256) : nullptr;
-  launch_grouped_fold(op, x, rows, count, gp, partials, tickets, out, S(stream));
+  float* round_vals = nullptr;
+  if (g->partitions > 1 && ws_bytes >= tiler_cuda_grouped_workspace_bytes(rows, g))
+    round_vals = (float*)((uint8_t*)ws + grouped_base_bytes(rows, g));
+  launch_grouped_fold(op, x, rows, count, gp, partials, tickets, round_vals, ctx->facts.sm_count, out, S(stream));
   return last_error_status();
 }
 
