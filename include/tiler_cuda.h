@@ -163,11 +163,8 @@ int32_t tiler_cuda_plan_grouping(const tiler_cuda_context* ctx, uint64_t rows, u
 /* The same proposal for a stated SM count, without a device (planning runs
  * on a build host in the reference: session::compile, session.rs:2587). */
 int32_t tiler_cuda_plan_grouping_for(int32_t sm_count, uint64_t rows, uint64_t count, tiler_cuda_grouping* out);
-/* allocate_dispatch (adapter.rs:672-674): workspace bytes for the grouped
- * fold: partials [rows*P] and per-row completion tickets (required, each
- * region padded to 256 bytes), then round totals [rows*P*rounds] (optional:
- * a workspace that holds them lets the round-parallel kernel run; results
- * are the same bits either way). */
+/* allocate_dispatch (adapter.rs:672-674): workspace bytes the grouped fold
+ * needs (partials + per-row completion tickets). */
 uint64_t tiler_cuda_grouped_workspace_bytes(uint64_t rows, const tiler_cuda_grouping* g);
 /* Grouped sum (tiler::strict-serial-sum-f32 realized under a declared
  * grouping; conformance against partitioned/cooperative references,

@@ -69,8 +69,7 @@ def test_grouped_workspace_bytes(native):
     L = native.lib()
     g = native.Grouping(partitions=1024, threads=512, k=4, rounds=8, combine_threads=512, combine_k=2,
                         combine_rounds=1)
-    # partials (4096 B) | tickets (one row, padded to 256 B) | round totals (1024 * 8 floats)
-    assert L.tiler_cuda_grouped_workspace_bytes(1, C.byref(g)) == 4096 + 256 + 1024 * 8 * 4
+    assert L.tiler_cuda_grouped_workspace_bytes(1, C.byref(g)) == 4096 + 4
     g.partitions = 1
     assert L.tiler_cuda_grouped_workspace_bytes(1, C.byref(g)) == 0
 

@@ -389,41 +389,7 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-#ifndef TILER_WAIT_HINT_NS
-#define TILER_WAIT_HINT_NS 100
-#endif
-#ifndef TILER_WAIT_MODE
-#define TILER_WAIT_MODE 0
-#endif
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(TILER_WAIT_HINT_NS)
-      : "memory");
-  return ok != 0;
-}
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, tiler_cuda_status* st) {
-#if TILER_WAIT_MODE == 1
-  if (mbar_test_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) break;
-  }
-  if (st) atomicAdd(&st->timeouts, 1u);
-  return false;
-#elif TILER_WAIT_MODE == 2
-  if (mbar_try_wait_hint(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_hint(bar, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) break;
-  }
-  if (st) atomicAdd(&st->timeouts, 1u);
-  return false;
-#else
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
@@ -432,7 +398,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, tiler_
   }
   if (st) atomicAdd(&st->timeouts, 1u);
   return false;
-#endif
 }
 
 // 1D bulk copy global -> shared, completing on an mbarrier (16-byte aligned

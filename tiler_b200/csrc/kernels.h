@@ -17,11 +17,8 @@ struct GroupedParams {
 };
 
 // reduce.cu
-// round_vals (nullable): rows * partitions * rounds floats of workspace that
-// enable the round-parallel kernel.
 void launch_grouped_fold(int op, const float* x, uint64_t rows, uint64_t count, const GroupedParams& gp,
-                         float* partials, unsigned int* tickets, float* round_vals, int sm_count, float* out,
-                         cudaStream_t stream);
+                         float* partials, unsigned int* tickets, float* out, cudaStream_t stream);
 void launch_strict_sum(const float* x, uint64_t rows, uint64_t count, float* out, cudaStream_t stream);
 void launch_partitioned_sum(const float* x, uint64_t rows, uint64_t count, uint64_t P, uint64_t per,
                             float* partials, float* out, cudaStream_t stream);

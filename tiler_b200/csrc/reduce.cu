@@ -92,26 +92,23 @@ __device__ float compose_block(const float* __restrict__ seq, uint64_t n, uint32
   return total;
 }
 
-// Runtime-k variant for the level-3 combine and small partitions.  The T
-// composition threads are virtual: warp w of the CTA plays composition warps
-// w, w + nwarps, ..., so the CTA may have fewer threads than T.
+// Runtime-k variant for the level-3 combine and small partitions.
 template <int OP>
 __device__ float compose_block_generic(const float* seq, uint64_t n, uint32_t T, uint32_t k, uint32_t R,
                                        float* slots, bool use_cg) {
-  const uint32_t G = T >> 5, tid = threadIdx.x, nwarps = blockDim.x >> 5;
+  const uint32_t G = T >> 5, tid = threadIdx.x;
   const uint32_t warp = tid >> 5, lane = tid & 31;
   const float ident = identity_value<OP>();
-  for (uint32_t vw = warp; vw < G; vw += nwarps) {
-    const uint32_t vt = vw * 32 + lane;
+  if (tid < T) {
     for (uint32_t r = 0; r < R; ++r) {
-      uint64_t base = ((uint64_t)r * T + vt) * k;
+      uint64_t base = ((uint64_t)r * T + tid) * k;
       float v = ident;
       for (uint32_t i = 0; i < k; ++i) {
         float c = base + i < n ? (use_cg ? __ldcg(seq + base + i) : seq[base + i]) : ident;
         v = i == 0 ? c : fold2<OP>(v, c);
       }
       v = butterfly<OP>(v);
-      if (lane == 0) slots[r * G + vw] = v;
+      if (lane == 0) slots[r * G + warp] = v;
     }
   }
   __syncthreads();
@@ -129,203 +126,6 @@ __device__ float compose_block_generic(const float* seq, uint64_t n, uint32_t T,
   }
   __syncthreads();
   return total;
-}
-
-// ---- round-parallel realization of the same grouping --------------------------
-//
-// The composition's rounds are independent until their totals are folded in
-// order, so a round (T*k contributors, 8 KB at T = 512, k = 4) is the unit
-// of work: one warp computes a round total exactly as the T-thread CTA would
-// (lane l of composition warp g folds its k contributors strictly, the
-// ascending butterfly, then the strict fold over the G warp slots), and the
-// totals go to the workspace.  Each SM runs one CTA over a contiguous range
-// of the rows x partitions x rounds sequence (balanced to within one round);
-// each warp streams its rounds through its own ring of shared-memory buffers
-// with one bulk copy per round.  The last CTA to finish folds every
-// partition's round totals in ascending order and then the partitions
-// (level 3), as the CTA-per-partition kernel does.  The results are the
-// same bits.
-#ifdef TILER_SUM_PROBE
-__device__ unsigned long long g_sum_probe[1024][4];
-#endif
-constexpr int kRoundThreads = 256;
-constexpr uint32_t kRoundSmemBytes = 192 * 1024;
-
-// The G composition warps' folds are independent until the slot fold, so
-// the warp runs all G butterflies in lockstep (G-way instruction-level
-// parallelism instead of G dependent shuffle chains).
-template <int OP, int K>
-__device__ __forceinline__ float round_total(const float* src, uint32_t nvalid, uint32_t G, uint32_t lane) {
-  constexpr uint32_t kMaxG = 32;
-  const float ident = identity_value<OP>();
-  float v[kMaxG];
-#pragma unroll
-  for (uint32_t g = 0; g < kMaxG; ++g) {
-    if (g < G) {
-      const uint32_t e = (g * 32 + lane) * K;
-      float vals[K];
-      if (e + K <= nvalid) {
-        if constexpr (K == 4) {
-          const float4 q = *reinterpret_cast<const float4*>(src + e);
-          vals[0] = q.x; vals[1] = q.y; vals[2] = q.z; vals[3] = q.w;
-        } else if constexpr (K == 2) {
-          const float2 q = *reinterpret_cast<const float2*>(src + e);
-          vals[0] = q.x; vals[1] = q.y;
-        } else {
-          vals[0] = src[e];
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < K; ++i) vals[i] = e + i < nvalid ? src[e + i] : ident;
-      }
-      v[g] = vals[0];
-#pragma unroll
-      for (int i = 1; i < K; ++i) v[g] = fold2<OP>(v[g], vals[i]);
-    }
-  }
-#pragma unroll
-  for (int m = 1; m < 32; m <<= 1) {
-#pragma unroll
-    for (uint32_t g = 0; g < kMaxG; ++g)
-      if (g < G) v[g] = fold2<OP>(v[g], __shfl_xor_sync(0xffffffffu, v[g], m));
-  }
-  float s = v[0];
-#pragma unroll
-  for (uint32_t g = 1; g < kMaxG; ++g)
-    if (g < G) s = fold2<OP>(s, v[g]);
-  return s;
-}
-
-template <int OP, int K>
-__global__ void __launch_bounds__(kRoundThreads, 1)
-    grouped_rounds_kernel(const float* __restrict__ x, uint64_t rows, uint64_t count, GroupedParams gp,
-                          float* __restrict__ round_vals, float* __restrict__ partials,
-                          unsigned int* __restrict__ ticket, float* __restrict__ out, uint32_t nbw) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  constexpr uint32_t kWarps = kRoundThreads / 32;
-  const uint32_t T = gp.threads, G = T / 32, warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const uint64_t P = gp.partitions, R = gp.rounds, per = count / P;
-  const uint32_t round_elems = T * K, round_bytes = round_elems * 4;
-  const uint64_t total = rows * P * R;
-  const uint64_t lo = blockIdx.x * total / gridDim.x, hi = (blockIdx.x + 1) * total / gridDim.x;
-  float* bufs = reinterpret_cast<float*>(smem_raw) + (uint64_t)warp * nbw * round_elems;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + (uint64_t)kWarps * nbw * round_bytes) + warp * nbw;
-  const uint64_t pol = policy_evict_first();
-
-  auto locate = [&](uint64_t q, const float** src, uint32_t* nvalid) {
-    const uint64_t row = q / (P * R), rem = q % (P * R), p = rem / R, j = rem % R;
-    const uint64_t start = j * round_elems;
-    *src = x + row * count + p * per + start;
-    *nvalid = (uint32_t)umin64(round_elems, per - start);
-  };
-  auto issue = [&](uint64_t kk) {  // the warp's kk-th round into buffer kk % nbw
-    const uint64_t q = lo + warp + kk * kWarps;
-    if (q >= hi) return;
-    const float* src;
-    uint32_t nvalid;
-    locate(q, &src, &nvalid);
-    const uint32_t b = (uint32_t)(kk % nbw);
-    mbar_arrive_expect_tx(&full[b], nvalid * 4);
-    bulk_g2s(bufs + (uint64_t)b * round_elems, src, nvalid * 4, &full[b], pol);
-  };
-#ifdef TILER_SUM_PROBE
-  if (threadIdx.x == 0) g_sum_probe[blockIdx.x][0] = global_ns();
-#endif
-  if (lane == 0) {
-    for (uint32_t b = 0; b < nbw; ++b) mbar_init(&full[b], 1);
-    fence_barrier_init();
-    for (uint32_t b = 0; b < nbw; ++b) issue(b);
-  }
-  __syncwarp();
-  bool direct = false;  // set when a copy did not land in time: read global memory instead
-  uint64_t kk = 0, kk_dead = 0;
-  for (uint64_t q = lo + warp; q < hi; q += kWarps, ++kk) {
-    const float* src;
-    uint32_t nvalid;
-    locate(q, &src, &nvalid);
-    const uint32_t b = (uint32_t)(kk % nbw);
-    if (!direct) {
-      const bool ok = mbar_wait(&full[b], (uint32_t)((kk / nbw) & 1), nullptr);
-      if (__any_sync(0xffffffffu, !ok)) {
-        direct = true;
-        kk_dead = kk;
-      }
-    }
-#ifdef TILER_SUM_PROBE_NO_COMPUTE
-    const float s = (direct ? src : bufs + (uint64_t)b * round_elems)[lane];
-#else
-    const float s = round_total<OP, K>(direct ? src : bufs + (uint64_t)b * round_elems, nvalid, G, lane);
-#endif
-    if (lane == 0) round_vals[q] = s;
-    __syncwarp();
-    if (lane == 0 && !direct) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(kk + nbw);
-    }
-  }
-  if (direct && lane == 0)  // copies issued before the first miss land before shared memory is released
-    for (uint64_t r = kk_dead; r < kk_dead + nbw && lo + warp + r * kWarps < hi; ++r)
-      (void)mbar_wait(&full[r % nbw], (uint32_t)((r / nbw) & 1), nullptr);
-
-#ifdef TILER_SUM_PROBE
-  if (lane == 0) atomicMax(&g_sum_probe[blockIdx.x][1], (unsigned long long)global_ns());
-#endif
-  __shared__ unsigned int is_last;
-  if (lane == 0) __threadfence();  // this warp's round totals before the CTA's ticket
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    is_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  float* slots = reinterpret_cast<float*>(smem_raw);
-  for (uint64_t row = 0; row < rows; ++row) {
-    const float* rv = round_vals + row * P * R;
-    if (P * R * 4 <= kRoundSmemBytes) {
-      // stage the row's round totals with coalesced loads, then fold each
-      // partition's totals in ascending order from shared memory
-      for (uint64_t i0 = threadIdx.x; i0 < P * R; i0 += 8 * (uint64_t)blockDim.x) {
-        float t[8];  // 8 loads in flight per thread
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint64_t i = i0 + u * (uint64_t)blockDim.x;
-          t[u] = i < P * R ? __ldcg(rv + i) : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint64_t i = i0 + u * (uint64_t)blockDim.x;
-          if (i < P * R) slots[i] = t[u];
-        }
-      }
-      __syncthreads();
-      rv = slots;
-    }
-    for (uint64_t p = threadIdx.x; p < P; p += blockDim.x) {
-      float v = rv[p * R];
-      for (uint64_t j = 1; j < R; ++j) v = fold2<OP>(v, rv[p * R + j]);
-      partials[row * P + p] = v;
-    }
-    __syncthreads();
-    const float* pr = partials + row * P;
-    float t;
-    if (gp.combine_threads == 0) {
-      t = 0.0f;
-      if (threadIdx.x == 0) {
-        t = pr[0];
-        for (uint64_t i = 1; i < P; ++i) t = fold2<OP>(t, pr[i]);
-      }
-    } else {
-      t = compose_block_generic<OP>(pr, P, gp.combine_threads, gp.combine_k, gp.combine_rounds, slots, true);
-    }
-    if (threadIdx.x == 0) out[row] = canon(t);
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) *ticket = 0;  // ready for the next launch
-#ifdef TILER_SUM_PROBE
-  if (threadIdx.x == 0) g_sum_probe[blockIdx.x][2] = global_ns();
-#endif
 }
 
 template <int OP, int K>
@@ -371,41 +171,8 @@ __global__ void __launch_bounds__(1024) grouped_fold_kernel(const float* __restr
   }
 }
 
-bool grouped_rounds_eligible(const float* x, uint64_t rows, uint64_t count, const GroupedParams& gp,
-                             int sm_count) {
-  if (gp.partitions <= 1 || sm_count <= 0) return false;
-  const uint64_t per = count / gp.partitions;
-  const uint64_t total = rows * gp.partitions * gp.rounds;
-  const uint64_t round_bytes = (uint64_t)gp.threads * gp.k * 4;
-  return (uintptr_t)x % 16 == 0 && count % 4 == 0 && per % 4 == 0 && round_bytes <= 16384 &&
-         total >= 8ull * (uint64_t)sm_count && total < (1ull << 40) &&
-         (uint64_t)gp.combine_rounds * (gp.combine_threads / 32 + 1) * 4 <= kRoundSmemBytes;
-}
-
 void launch_grouped_fold(int op, const float* x, uint64_t rows, uint64_t count, const GroupedParams& gp,
-                         float* partials, unsigned int* tickets, float* round_vals, int sm_count, float* out,
-                         cudaStream_t stream) {
-  if (round_vals && grouped_rounds_eligible(x, rows, count, gp, sm_count)) {
-    const uint32_t round_bytes = gp.threads * gp.k * 4;
-    constexpr uint32_t W = kRoundThreads / 32;
-    const uint32_t nbw = std::max<uint32_t>(1, kRoundSmemBytes / (round_bytes * W));
-    const size_t smem = (size_t)W * nbw * (round_bytes + 8);
-    const unsigned grid = (unsigned)sm_count;
-    auto go = [&](auto kern) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      kern<<<grid, kRoundThreads, smem, stream>>>(x, rows, count, gp, round_vals, partials, tickets, out, nbw);
-    };
-    if (op == 0) {
-      if (gp.k == 4) go(grouped_rounds_kernel<0, 4>);
-      else if (gp.k == 2) go(grouped_rounds_kernel<0, 2>);
-      else go(grouped_rounds_kernel<0, 1>);
-    } else {
-      if (gp.k == 4) go(grouped_rounds_kernel<1, 4>);
-      else if (gp.k == 2) go(grouped_rounds_kernel<1, 2>);
-      else go(grouped_rounds_kernel<1, 1>);
-    }
-    return;
-  }
+                         float* partials, unsigned int* tickets, float* out, cudaStream_t stream) {
   const uint32_t G = gp.threads / 32;
   uint32_t R = gp.rounds;
   uint32_t cR = gp.combine_threads ? gp.combine_rounds : 0;
