@@ -39,6 +39,9 @@ int init_exp_table(int device) {
     host[j][1] = lo;
   }
   if (cudaMemcpyToSymbol(g_exp2_table, host, sizeof(host)) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
+  double hi_col[256];
+  for (int j = 0; j < 256; ++j) hi_col[j] = host[j][0];
+  if (cudaMemcpyToSymbol(g_exp2_hi, hi_col, sizeof(hi_col)) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
   g_table_ready[device] = true;
   return TILER_CUDA_OK;
 }

@@ -78,10 +78,11 @@ __device__ __forceinline__ void report_undecided(tiler_cuda_status* s) {
 // reference's UndecidedTranscendentalReference refusal.
 //
 // The 2^(j/256) table (hi + lo doubles) is written once per device by the
-// host runtime (runtime.cu, from __float128 exp2q) into g_exp2_table; the fast
+// host runtime (abi.cu, from __float128 exp2q) into g_exp2_table; the fast
 // path reads its hi column from a shared-memory copy.
 
 __device__ double g_exp2_table[256][2];
+__device__ double g_exp2_hi[256];  // the hi column again, contiguous (read where no shared copy is kept)
 
 // 256/ln2 and ln2/256 split so that n*kLn2By256Hi is exact for |n| < 2^17.
 constexpr double kInvLn2x256 = 369.3299304675746271;            // 256 / ln 2 (rounded)
@@ -326,6 +327,23 @@ __device__ __forceinline__ uint16_t silu_bf16_epilogue(float x, const double* ta
     const bool normal = ((b >> 23) & 0xffu) != 0;
     if (normal && (float)dist > 2.0f * ax + 24.0f) return (uint16_t)((b + 0x7fffu + ((b >> 16) & 1u)) >> 16);
   }
+  return f32_to_bf16(silu_cr_fast(x, table_hi, st));
+}
+
+// The same decision split in two for a warp draining 32 accumulators per
+// lane: silu_bf16_fast returns the bf16 bits of the approximation and sets
+// *certain when they are provably those of the certified value; the rare
+// uncertain elements are then redone by silu_bf16_certified in one
+// warp-uniform branch, so the common path has no per-element branch.
+__device__ __forceinline__ uint32_t silu_bf16_fast(float x, bool* certain) {
+  const float ax = fabsf(x);
+  const float y = __fdividef(x, __fadd_rn(1.0f, __expf(-x)));
+  const uint32_t b = __float_as_uint(y);
+  const float dist = fabsf(__fsub_rn((float)(int)(b & 0xffffu), 32768.0f));
+  *certain = ax < 80.0f && ((b >> 23) & 0xffu) != 0 && dist > __fadd_rn(__fmul_rn(2.0f, ax), 24.0f);
+  return (b + 0x7fffu + ((b >> 16) & 1u)) >> 16;
+}
+__device__ __noinline__ uint32_t silu_bf16_certified(float x, const double* table_hi, tiler_cuda_status* st) {
   return f32_to_bf16(silu_cr_fast(x, table_hi, st));
 }
 

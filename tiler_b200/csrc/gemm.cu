@@ -15,8 +15,11 @@
 //                 K=16) and tcgen05.commit back to the ring / accumulators;
 //      warps 2-9  epilogue (two per TMEM lane quarter, half the columns each):
 //                 tcgen05.ld 32 columns at a time, the SiLU of
-//                 silu.rs:158-180 (certified exp), RNE to bf16, 16-byte
-//                 stores; accumulator b of tile i+1 fills while tile i drains.
+//                 silu.rs:158-180 (hardware exp/divide with a certified
+//                 fallback for the rare values near a bf16 rounding
+//                 boundary, one warp-uniform branch), RNE to bf16, into a
+//                 32x64 swizzled shared-memory box that one TMA store writes
+//                 to C; accumulator b of tile i+1 fills while tile i drains.
 //    Every mbarrier wait is bounded; a wait that gives up records a timeout
 //    in the status word and the CTA stops, frees its TMEM and returns.
 #include "common.cuh"
@@ -68,6 +71,11 @@ constexpr int kGemmEpiWarps = 8;  // two per TMEM lane quarter, each draining ha
 constexpr int kGemmThreads = 32 * (2 + kGemmEpiWarps);
 constexpr uint32_t kTmemCols = 512;
 
+// Epilogue staging: per epilogue warp one 32-row x 64-column bf16 box
+// (4 KB, 128-byte swizzle) that a TMA store writes to C.
+constexpr int kEpiBoxCols = 64;
+constexpr int kEpiStageBytes = 32 * kEpiBoxCols * 2;
+
 struct GemmBars {
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -76,8 +84,8 @@ struct GemmBars {
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes + 2048 /*exp table*/ +
-                             sizeof(GemmBars) + 64;
+constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + (size_t)kStages * kStageBytes +
+                             (size_t)kGemmEpiWarps * kEpiStageBytes + sizeof(GemmBars) + 64;
 
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): K-major,
 // 128-byte swizzle, 8-row core groups 1024 bytes apart.
@@ -122,18 +130,17 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                             uint32_t m_blocks, uint32_t n_blocks, uint32_t k_blocks, int epilogue,
-                             uint16_t* __restrict__ c, uint64_t ldc, tiler_cuda_status* st) {
+                             const __grid_constant__ CUtensorMap tmap_c, uint32_t m_blocks, uint32_t n_blocks,
+                             uint32_t k_blocks, int epilogue, tiler_cuda_status* st) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = ((raw + 1023) & ~1023u) - raw;
   uint8_t* tiles = smem_raw + pad;
-  double* table = reinterpret_cast<double*>(tiles + (size_t)kStages * kStageBytes);
-  GemmBars& B = *reinterpret_cast<GemmBars*>(tiles + (size_t)kStages * kStageBytes + 2048);
+  uint8_t* epi_stage = tiles + (size_t)kStages * kStageBytes;  // 1024-byte aligned
+  GemmBars& B = *reinterpret_cast<GemmBars*>(epi_stage + (size_t)kGemmEpiWarps * kEpiStageBytes);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t num_tiles = m_blocks * n_blocks;
 
-  load_exp_table(table);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) { mbar_init(&B.full[s], 1); mbar_init(&B.empty[s], 1); }
     for (int s = 0; s < 2; ++s) { mbar_init(&B.tmem_full[s], 1); mbar_init(&B.tmem_empty[s], 32 * kGemmEpiWarps); }
@@ -198,7 +205,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // epilogue warps 2..9: TMEM lane quarter (warp % 4), column half (warp - 2) / 4
     const uint32_t quarter = warp & 3;
     const uint32_t col0 = ((warp - 2) / 4) * (kBN / 2);
-    const uint32_t row_in_tile = quarter * 32 + lane;
+    uint8_t* stage = epi_stage + (size_t)(warp - 2) * kEpiStageBytes;
+    const uint32_t stage_u32 = smem_u32(stage);
     uint32_t local = 0;
     for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const uint32_t mb = tile % m_blocks, nb = tile / m_blocks;
@@ -206,34 +214,65 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&B.tmem_full[buf], (local >> 1) & 1, st)) { *abort_flag = 1; break; }
       if (*abort_flag) break;
       tmem_fence_after();
-      const uint64_t row = (uint64_t)mb * kBM + row_in_tile;
-      uint16_t* crow = c + row * ldc + (uint64_t)nb * kBN;
 #pragma unroll 1
-      for (uint32_t col = col0; col < col0 + (uint32_t)kBN / 2; col += 32) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + buf * kBN + col;
-        TMEM_LD32(taddr, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        uint32_t packed[16];
-        if (epilogue == 1) {
+      for (uint32_t box = col0; box < col0 + (uint32_t)kBN / 2; box += kEpiBoxCols) {
+        // the previous box's store has finished reading the staging buffer
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
+#pragma unroll 1
+        for (uint32_t half = 0; half < 2; ++half) {
+          uint32_t r[32];
+          const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + buf * kBN + box + half * 32;
+          TMEM_LD32(taddr, r);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (epilogue == 1) {
+            uint32_t uncertain = 0;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            packed[j] = (uint32_t)silu_bf16_epilogue(__uint_as_float(r[2 * j]), table, st) |
-                        ((uint32_t)silu_bf16_epilogue(__uint_as_float(r[2 * j + 1]), table, st) << 16);
-        } else {
+            for (int j = 0; j < 32; ++j) {
+              bool certain;
+              const uint32_t bits = silu_bf16_fast(__uint_as_float(r[j]), &certain);
+              uncertain |= (certain ? 0u : 1u) << j;
+              r[j] = bits;
+            }
+            if (__any_sync(0xffffffffu, uncertain != 0)) {
+              // rare: reload the accumulators and certify the flagged ones
+              uint32_t x[32];
+              TMEM_LD32(taddr, x);
+              asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            packed[j] = (uint32_t)f32_to_bf16(canon(__uint_as_float(r[2 * j]))) |
-                        ((uint32_t)f32_to_bf16(canon(__uint_as_float(r[2 * j + 1]))) << 16);
+              for (int j = 0; j < 32; ++j)
+                if ((uncertain >> j) & 1u) r[j] = silu_bf16_certified(__uint_as_float(x[j]), g_exp2_hi, st);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = f32_to_bf16(canon(__uint_as_float(r[j])));
+          }
+          // row `lane` of the box: 16-byte chunk c (of 8) at c ^ (row & 7)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t chunk = half * 4 + q;
+            const uint32_t off = lane * 128 + ((chunk ^ (lane & 7)) * 16);
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stage_u32 + off),
+                         "r"(r[8 * q] | (r[8 * q + 1] << 16)), "r"(r[8 * q + 2] | (r[8 * q + 3] << 16)),
+                         "r"(r[8 * q + 4] | (r[8 * q + 5] << 16)), "r"(r[8 * q + 6] | (r[8 * q + 7] << 16))
+                         : "memory");
+          }
         }
-        uint4* dst = reinterpret_cast<uint4*>(crow + col);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          const int32_t x = (int32_t)(nb * kBN + box), y = (int32_t)(mb * kBM + quarter * 32);
+          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(&tmap_c),
+                       "r"(x), "r"(y), "r"(stage_u32)
+                       : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
       }
       tmem_fence_before();
       mbar_arrive(&B.tmem_empty[buf]);
     }
+    // the stores have completed before the CTA (and its shared memory) goes away
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   tmem_fence_before();
   __syncthreads();
@@ -254,13 +293,17 @@ int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t 
                      uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
   if (m % kBM || n % kBN || k % kBK || k == 0) return TILER_CUDA_UNSUPPORTED;
   if ((uintptr_t)a % 16 || (uintptr_t)b % 16 || (uintptr_t)c % 16 || ldc % 8 || ldc < n) return TILER_CUDA_UNSUPPORTED;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tcm;
   if (!make_tmap(&ta, a, m, k, kBM) || !make_tmap(&tb, b, n, k, kBN)) return TILER_CUDA_DEVICE_ERROR;
+  // C [m, n] bf16 row-major with row pitch ldc: 64 x 32 boxes, 128-byte swizzle
+  if (!make_tmap_2d(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c, n, m, ldc * 2, (uint32_t)kEpiBoxCols, 32,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return TILER_CUDA_DEVICE_ERROR;
   const uint32_t mbk = (uint32_t)(m / kBM), nbk = (uint32_t)(n / kBN), kbk = (uint32_t)(k / kBK);
   const uint32_t tiles = mbk * nbk;
   const unsigned grid = std::min<uint32_t>(tiles, (uint32_t)sm_count);
   cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
-  gemm_bf16_tcgen05_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(ta, tb, mbk, nbk, kbk, epilogue, c, ldc, st);
+  gemm_bf16_tcgen05_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(ta, tb, tcm, mbk, nbk, kbk, epilogue, st);
   return TILER_CUDA_OK;
 }
 
