@@ -215,6 +215,22 @@ int32_t tiler_cuda_rms_norm_bf16(tiler_cuda_context* ctx, void* stream, tiler_cu
                                  const uint16_t* x,
                                  const uint16_t* w, int64_t w_row_stride, uint64_t rows,
                                  uint64_t extent, uint32_t eps_bits, uint16_t* y);
+/* RMS normalization of HOST rows: the dispatch path that uploads the
+ * caller's input, launches and reads the output back
+ * (prototypes/candle-metal-adapter/src/adapter.rs:1311-1384, allocate_dispatch
+ * + dispatch), chunked so the upload of chunk i+1, the kernel on chunk i and
+ * the download of chunk i-1 overlap (the copy engines are full duplex).
+ * dtype 0 = f32, 1 = bf16.  x_host / y_host should be pinned (page-locked)
+ * for the copies to run asynchronously; x_dev / y_dev are device buffers of
+ * rows*extent elements owned by the caller (the library allocates nothing);
+ * w is on the device ([extent], or [rows, extent] with w_row_stride =
+ * extent).  chunk_rows 0 lets the library choose; at most 32 chunks.  The
+ * whole operation is ordered after the work already on `stream`, and work
+ * enqueued on `stream` afterwards sees y_host complete. */
+int32_t tiler_cuda_rms_norm_host(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status, int32_t dtype,
+                                 const void* x_host, void* x_dev, const void* w, int64_t w_row_stride,
+                                 uint64_t rows, uint64_t extent, uint32_t eps_bits, void* y_dev, void* y_host,
+                                 uint64_t chunk_rows);
 /* SoftmaxF32Reference (softmax.rs:99-137, :260-315) over the last axis.
  * causal_period > 0 adds -inf where col > (row_offset + row) % causal_period
  * (the program's upstream add-f32 of a broadcast mask, standard.rs:211-221). */

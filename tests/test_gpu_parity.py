@@ -319,6 +319,21 @@ def test_quantize_refusals(fam):
     assert e.value.code == 9 and e.value.position == 0
 
 
+@pytest.mark.parametrize("dtype,rows,extent,chunk", [(torch.float32, 8192, 4096, 0), (torch.float32, 1000, 1024, 300),
+                                                    (torch.bfloat16, 777, 4096, 100)])
+def test_rms_norm_host_buffers_match_the_device_path(fam, dtype, rows, extent, chunk):
+    # chunked upload / kernel / download gives the device path's bits, for a
+    # broadcast weight row and for a per-row weight matrix
+    gen = torch.Generator().manual_seed(rows)
+    x = torch.randn(rows, extent, generator=gen).to(dtype).pin_memory()
+    for w_full in (False, True):
+        w = (torch.rand((rows, extent) if w_full else (extent,), generator=gen) + 0.5).to(dtype).cuda()
+        want = fam.rms_norm(x.cuda(), w).cpu()
+        got = fam.rms_norm_host(x, w, chunk_rows=chunk)
+        assert torch.equal(got.view(torch.int16 if dtype == torch.bfloat16 else torch.int32),
+                           want.view(torch.int16 if dtype == torch.bfloat16 else torch.int32))
+
+
 def test_quantize_staged_rows_refusals_and_extremes(fam, oracle_lib):
     # 4096-wide rows take the shared-memory staged kernel: the first NaN of
     # the earliest refused row is reported, and extreme magnitudes (largest

@@ -15,6 +15,9 @@
 struct tiler_cuda_context {
   int device;
   tiler_cuda_device_facts facts;
+  // copy streams and events of the host-buffer entry points (made on first use)
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t ev[2 * 32 + 2] = {};
 };
 
 namespace {
@@ -187,6 +190,18 @@ int32_t tiler_cuda_context_create(int32_t device, tiler_cuda_context** out) {
 }
 
 int32_t tiler_cuda_context_destroy(tiler_cuda_context* ctx) {
+  if (ctx && ctx->copy_in) {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->copy_in);
+    cudaStreamSynchronize(ctx->copy_out);
+    for (cudaEvent_t e : ctx->ev)
+      if (e) cudaEventDestroy(e);
+    cudaStreamDestroy(ctx->copy_in);
+    cudaStreamDestroy(ctx->copy_out);
+    if (cur >= 0) cudaSetDevice(cur);
+  }
   delete ctx;
   return TILER_CUDA_OK;
 }
@@ -425,6 +440,63 @@ int32_t tiler_cuda_rms_norm_f32(tiler_cuda_context* ctx, void* stream, tiler_cud
                                 const float* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,
                                 uint32_t eps_bits, float* y) {
   return rms(0, ctx, stream, st, x, w, w_row_stride, rows, extent, eps_bits, y);
+}
+
+static int32_t ensure_copy_streams(tiler_cuda_context* ctx) {
+  if (ctx->copy_in) return TILER_CUDA_OK;
+  if (cudaStreamCreateWithFlags(&ctx->copy_in, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->copy_out, cudaStreamNonBlocking) != cudaSuccess)
+    return TILER_CUDA_DEVICE_ERROR;
+  for (cudaEvent_t& e : ctx->ev)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
+  return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_rms_norm_host(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st, int32_t dtype,
+                                 const void* x_host, void* x_dev, const void* w, int64_t w_row_stride,
+                                 uint64_t rows, uint64_t extent, uint32_t eps_bits, void* y_dev, void* y_host,
+                                 uint64_t chunk_rows) {
+  CHECK_CTX(ctx);
+  if (dtype != 0 && dtype != 1) return TILER_CUDA_UNSUPPORTED;
+  if (!eps_admitted(eps_bits) || w_row_stride < 0) return TILER_CUDA_INVALID_APPLICATION;
+  if (extent > (1ull << 24)) return TILER_CUDA_SHAPE_TOO_LARGE;
+  if (rows == 0 || extent == 0) return TILER_CUDA_OK;
+  if (!x_host || !x_dev || !w || !y_dev || !y_host) return TILER_CUDA_INVALID_APPLICATION;
+  if (w_row_stride != 0 && (uint64_t)w_row_stride != extent) return TILER_CUDA_UNSUPPORTED;
+  int32_t r = ensure_copy_streams(ctx);
+  if (r != TILER_CUDA_OK) return r;
+  constexpr uint64_t kMaxChunks = 32;
+  if (chunk_rows == 0) chunk_rows = std::max<uint64_t>(1, (rows + 7) / 8);
+  chunk_rows = std::max(chunk_rows, (rows + kMaxChunks - 1) / kMaxChunks);
+  const uint64_t esize = dtype ? 2 : 4, row_bytes = extent * esize;
+  float eps;
+  memcpy(&eps, &eps_bits, 4);
+  cudaStream_t s = S(stream);
+  cudaEvent_t* ev = ctx->ev;
+  // everything below runs after the work already on `stream`
+  if (cudaEventRecord(ev[0], s) != cudaSuccess || cudaStreamWaitEvent(ctx->copy_in, ev[0], 0) != cudaSuccess)
+    return TILER_CUDA_DEVICE_ERROR;
+  uint32_t k = 0;
+  for (uint64_t r0 = 0; r0 < rows; r0 += chunk_rows, ++k) {
+    const uint64_t n = std::min(chunk_rows, rows - r0);
+    const uint64_t off = r0 * row_bytes, bytes = n * row_bytes;
+    cudaEvent_t in_done = ev[2 + 2 * k], out_ready = ev[3 + 2 * k];
+    if (cudaMemcpyAsync((uint8_t*)x_dev + off, (const uint8_t*)x_host + off, bytes, cudaMemcpyHostToDevice,
+                        ctx->copy_in) != cudaSuccess ||
+        cudaEventRecord(in_done, ctx->copy_in) != cudaSuccess || cudaStreamWaitEvent(s, in_done, 0) != cudaSuccess)
+      return TILER_CUDA_DEVICE_ERROR;
+    const uint8_t* wc = (const uint8_t*)w + (w_row_stride ? off : 0);
+    launch_rms_norm(dtype, (const uint8_t*)x_dev + off, wc, w_row_stride, n, extent, eps, (uint8_t*)y_dev + off, st,
+                    ctx->facts.sm_count, s);
+    if (cudaEventRecord(out_ready, s) != cudaSuccess || cudaStreamWaitEvent(ctx->copy_out, out_ready, 0) != cudaSuccess ||
+        cudaMemcpyAsync((uint8_t*)y_host + off, (const uint8_t*)y_dev + off, bytes, cudaMemcpyDeviceToHost,
+                        ctx->copy_out) != cudaSuccess)
+      return TILER_CUDA_DEVICE_ERROR;
+  }
+  // work enqueued on `stream` afterwards sees every chunk downloaded
+  if (cudaEventRecord(ev[1], ctx->copy_out) != cudaSuccess || cudaStreamWaitEvent(s, ev[1], 0) != cudaSuccess)
+    return TILER_CUDA_DEVICE_ERROR;
+  return last_error_status();
 }
 
 int32_t tiler_cuda_rms_norm_bf16(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st, const uint16_t* x,

@@ -224,6 +224,34 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, out
     return y
 
 
+def rms_norm_host(x_host: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, out=None, x_dev=None,
+                  y_dev=None, chunk_rows: int = 0, check=True) -> torch.Tensor:
+    """RMS norm of host rows (tiler_cuda_rms_norm_host): chunked upload,
+    kernel and download overlapped on the copy engines.  ``x_host`` (and
+    ``out``) should be pinned; ``x_dev`` / ``y_dev`` are device staging
+    tensors of x's shape (made here when not given); ``w`` is on the device.
+    Returns the host output after the copies have completed."""
+    assert x_host.device.type == "cpu" and x_host.dtype in (torch.float32, torch.bfloat16)
+    assert x_host.is_contiguous() and (out is None or (out.device.type == "cpu" and out.is_contiguous()))
+    assert w.is_cuda and w.dtype == x_host.dtype
+    extent = x_host.shape[-1]
+    rows = x_host.numel() // extent if extent else 0
+    stride = 0 if w.dim() == 1 else extent
+    y = torch.empty(x_host.shape, dtype=x_host.dtype, pin_memory=True) if out is None else out
+    xd = torch.empty(x_host.shape, dtype=x_host.dtype, device=w.device) if x_dev is None else x_dev
+    yd = torch.empty_like(xd) if y_dev is None else y_dev
+    st = _status() if check else None
+    _check(N.lib().tiler_cuda_rms_norm_host(context(), _stream(), st.ptr if st else 0,
+                                            0 if x_host.dtype == torch.float32 else 1, x_host.data_ptr(), _ptr(xd),
+                                            _ptr(w), stride, rows, extent, eps_bits, _ptr(yd), y.data_ptr(),
+                                            chunk_rows),
+           "rms_norm_host")
+    torch.cuda.current_stream().synchronize()
+    if st:
+        _raise_from(st, "rms_norm_host")
+    return y
+
+
 def softmax(x: torch.Tensor, causal_period: int = 0, row_offset: int = 0, out=None, check=True) -> torch.Tensor:
     """SoftmaxF32Reference over the last axis (softmax.rs:99-137, :260-315);
     ``causal_period`` > 0 applies the block-causal additive -inf mask."""
