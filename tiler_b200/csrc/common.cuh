@@ -256,6 +256,32 @@ __device__ __forceinline__ float exp_cr_fast(float x, const double* table_hi, ti
   return exp_cr(x, table_hi, st);
 }
 
+// exp_cr_fast without its fallback, for callers that batch the rare
+// undecided arguments into one warp-uniform branch: returns the binary32
+// bits of e^x and sets *ok when they are certified (normal binary32 result,
+// binary64 value farther than 64 units of 2^-46 from a rounding midpoint);
+// otherwise the caller must take exp_cr(x).  The rounding to binary32 is
+// done on the bits: the candidate is 29 bits beyond binary32 precision and
+// not at a midpoint, so bit 28 of the low word decides it.
+__device__ __forceinline__ uint32_t exp_cr_bits(float x, const double* table_hi, bool* ok) {
+  const double xd = (double)x;
+  const double t = __fma_rn(xd, kInvLn2x256, kRoundShift);
+  const int n = __double2loint(t);
+  const double nd = __dsub_rn(t, kRoundShift);
+  double r = __fma_rn(-nd, kLn2By256Hi, xd);
+  r = __fma_rn(-nd, kLn2By256Mid, r);
+  double q = __fma_rn(r, 1.0 / 24.0, 1.0 / 6.0);
+  q = __fma_rn(r, q, 0.5);
+  const double p = __fma_rn(__dmul_rn(r, r), q, r);
+  const double tj = table_hi[n & 255];
+  const double y0 = __fma_rn(tj, p, tj);
+  const int hi = __double2hiint(y0) + ((n >> 8) << 20);
+  const uint32_t lo = (uint32_t)__double2loint(y0);
+  const int d = (int)(lo & 0x1fffffffu) - 0x10000000;
+  *ok = hi >= 0x38100000 && hi < 0x47f00000 && (d > 64 || d < -64);
+  return ((uint32_t)(hi - 0x38000000) << 3) + (lo >> 29) + ((lo >> 28) & 1u);
+}
+
 // Correctly rounded binary32 1/sqrt(t) (certified_rsqrt_strict,
 // rms_norm.rs:238-293).  The binary64 candidate is checked exactly: f is the
 // correctly rounded value iff mlo^2 t < 1 < mhi^2 t for the midpoints mlo,

@@ -493,6 +493,13 @@ __device__ __forceinline__ float max_nan(float a, float b) {
   return d;
 }
 
+// e^sh for the group kernel's flagged arguments (out of the fast path's
+// range, NaN, or near a rounding midpoint); kept out of line so the fast
+// path's registers are not sized for it.
+__device__ __noinline__ float softmax_exp_slow(float sh, const double* table, tiler_cuda_status* st) {
+  return sh > -104.0f ? exp_cr(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
+}
+
 __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM)
     softmax_group_kernel(const float* __restrict__ x, uint64_t rows, uint64_t extent, uint64_t period,
                          uint64_t row_offset, float* __restrict__ y, uint32_t group, tiler_cuda_status* st) {
@@ -529,6 +536,9 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
   for (uint64_t g = 0; g < ngroups; ++g) {
     const uint64_t row0 = group_row0(g);
     const uint32_t n = (uint32_t)umin64(G, rows - row0);
+#ifdef TILER_SMX_PROBE_TIMES
+    const long long t0 = clock64();
+#endif
     // each row warp loads its own row; its previous bulk store must have
     // finished reading the buffer first
     bool ok = true;
@@ -541,7 +551,7 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
       ok = mbar_wait(&full[warp], (uint32_t)(g & 1), st);
     }
 #ifdef TILER_SMX_PROBE_TIMES
-    long long t0 = clock64(), t1 = t0;
+    const long long t1 = clock64();
 #endif
 
     if (!chain_warp && warp < n) {
@@ -573,17 +583,23 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
         const float sh = __fsub_rn(xv, m);
         return sh > -104.0f ? exp_cr_fast(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
       };
-      uint32_t v = lane;
-      for (; v + 32 < live4; v += 64) {  // two vectors per lane: eight independent exps
-        const float4 q0 = b4[v], q1 = b4[v + 32];
-        const float4 r0 = make_float4(exp_of(q0.x), exp_of(q0.y), exp_of(q0.z), exp_of(q0.w));
-        const float4 r1 = make_float4(exp_of(q1.x), exp_of(q1.y), exp_of(q1.z), exp_of(q1.w));
-        b4[v] = r0;
-        b4[v + 32] = r1;
-      }
-      if (v < live4) {
-        const float4 q0 = b4[v];
-        b4[v] = make_float4(exp_of(q0.x), exp_of(q0.y), exp_of(q0.z), exp_of(q0.w));
+      for (uint32_t v = lane; v < live4; v += 32) {  // four independent exps per lane
+        const float4 q = b4[v];
+        const float xs[4] = {q.x, q.y, q.z, q.w};
+        uint32_t e[4], flagged = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float sh = __fsub_rn(xs[i], m);
+          bool ok;
+          e[i] = exp_cr_bits(sh, table, &ok);
+          flagged |= ((ok && sh > -104.0f) ? 0u : 1u) << i;
+        }
+        if (__any_sync(__activemask(), flagged != 0)) {  // rare: certify or special-case the flagged ones
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if ((flagged >> i) & 1u) e[i] = __float_as_uint(softmax_exp_slow(__fsub_rn(xs[i], m), table, st));
+        }
+        b4[v] = make_float4(__uint_as_float(e[0]), __uint_as_float(e[1]), __uint_as_float(e[2]), __uint_as_float(e[3]));
       }
       for (uint32_t c = live4 * 4 + lane; c < live; c += 32) b[c] = exp_of(b[c]);
       for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) b[c] = 0.0f;
@@ -648,8 +664,11 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
         const float nanv = __uint_as_float(kCanonicalNan);
         for (uint32_t v = lane; v < ext / 4; v += 32) b4[v] = make_float4(nanv, nanv, nanv, nanv);
       } else {
-        // e is finite and >= 0 and r finite: the product is never NaN
-        for (uint32_t v = lane; v < ext / 4; v += 32) {
+        // e is finite and >= 0 and r finite: the product is never NaN; the
+        // masked tail already holds zeros (0 * r = +0)
+        const uint64_t row_live = causal ? umin64((row_offset + row) % period + 1, extent) : extent;
+        const uint32_t nv = (uint32_t)((row_live + 3) / 4);
+        for (uint32_t v = lane; v < nv; v += 32) {
           const float4 q = b4[v];
           b4[v] = make_float4(__fmul_rn(q.x, r), __fmul_rn(q.y, r), __fmul_rn(q.z, r), __fmul_rn(q.w, r));
         }
@@ -676,9 +695,11 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
     }
 #endif
 #ifdef TILER_SMX_PROBE_TIMES
-    if (threadIdx.x == 0 && blockIdx.x == 100 && g < 8) {
-      long long* T = reinterpret_cast<long long*>(st) + 8;  // probe scratch after the status word
-      T[g * 4 + 0] = t1 - t0; T[g * 4 + 1] = t2 - t1; T[g * 4 + 2] = t3 - t2; T[g * 4 + 3] = t4 - t3;
+    if (threadIdx.x == 0) {  // phase cycles summed over all groups (probe scratch after the status word)
+      unsigned long long* T = reinterpret_cast<unsigned long long*>(st) + 8;
+      atomicAdd(&T[0], (unsigned long long)(t1 - t0)); atomicAdd(&T[1], (unsigned long long)(t2 - t1));
+      atomicAdd(&T[2], (unsigned long long)(t3 - t2)); atomicAdd(&T[3], (unsigned long long)(t4 - t3));
+      atomicAdd(&T[4], 1ull);
     }
 #endif
   }
