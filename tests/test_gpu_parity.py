@@ -284,7 +284,10 @@ def test_scale_bias_matches_oracle(fam, oracle_lib):
     assert_bits_equal(got, want)
 
 
-@pytest.mark.parametrize("rows,extent", [(16384, 4096), (3, 1001)])
+# shapes on both sides of the staged kernels' limits: quantize stages rows of
+# at most 16 KB with extent % 4 == 0; decode stages extent % 16 == 0 up to 4096
+@pytest.mark.parametrize("rows,extent", [(16384, 4096), (3, 1001), (37, 4096), (5, 4100), (9, 4092), (4, 8192),
+                                         (300, 16), (2, 4)])
 def test_quantize_decode_match_oracle(fam, oracle_lib, rows, extent):
     x = seeded_normal(rows, rows * extent).reshape(rows, extent)
     codes, scales = fam.quantize_i8_rows(cuda(x))
@@ -381,6 +384,20 @@ def test_gemm_bf16_silu_matches_oracle(fam, oracle_lib, m, n, k):
         want = oracle_lib.bf16_to_f32(want)
         err = np.abs(got - want) / np.maximum(np.abs(want), 1e-2)
         assert err.max() <= 1e-2, f"{epi}: max rel err {err.max()}"
+
+
+def test_gemm_bf16_writes_a_strided_output_inside_its_columns(fam):
+    # C with a row pitch wider than n (ldc = n + 256): the TMA-stored boxes land
+    # in C's columns only; the padding keeps its sentinel
+    m, n, k = 256, 512, 256
+    gen = torch.Generator("cuda").manual_seed(11)
+    a = (torch.randn(m, k, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    b = (torch.randn(n, k, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    want = fam.gemm_bf16(a, b, epilogue="silu")
+    wide = torch.full((m, n + 256), -7.0, device="cuda", dtype=torch.bfloat16)
+    got = fam.gemm_bf16(a, b, epilogue="silu", out=wide[:, :n])
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert (wide[:, n:] == -7.0).all()
 
 
 def test_gemm_bf16_full_config_sampled_rows(fam, oracle_lib):
