@@ -221,6 +221,35 @@ def test_rms_norm_bf16_matches_oracle(fam, oracle_lib, rows, extent):
     assert (got == want).all(), f"{(got != want).sum()} bf16 mismatches"
 
 
+def test_rms_norm_bf16_special_values_match_oracle(fam, oracle_lib):
+    # rows whose outputs are NaN (NaN or inf input), overflow to inf (huge
+    # weight), fall to bf16 subnormals (one huge and many tiny inputs), are
+    # all zero, or sit on bf16 rounding ties; per-row weights
+    extent = 4096
+    rows = 8
+    base = seeded_normal(41, rows * extent).reshape(rows, extent)
+    x = base.copy()
+    w = np.ones((rows, extent), np.float32)
+    x[0, 17] = np.nan
+    x[1, 3000] = np.inf
+    w[2, :] = 3.0e38
+    x[3, :] = 1e-30
+    x[3, 5] = 1e30
+    x[4, :] = 0.0
+    x[5, :] = -x[5, :]
+    w[6, :] = np.float32(1.0) + np.float32(2.0 ** -8)  # products land on bf16 ties often
+    x[7, ::2] = np.float32(2.0 ** -126)
+    xb = oracle_lib.f32_to_bf16(x)
+    wb = oracle_lib.f32_to_bf16(w)
+    xt = cuda(xb.view(np.int16)).view(torch.bfloat16)
+    wt = cuda(wb.view(np.int16)).view(torch.bfloat16)
+    got = host(fam.rms_norm(xt, wt).view(torch.int16)).view(np.uint16)
+    st, want = oracle_lib.rms_norm_bf16(xb, wb)
+    assert st == 0
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, f"{len(bad)} mismatches, first {bad[:4].tolist()}: {got[tuple(bad[0])]:#x} vs {want[tuple(bad[0])]:#x}"
+
+
 @pytest.mark.parametrize("rows,extent,period", [(2048, 2048, 2048), (64, 2048, 0), (33, 1000, 0), (16, 8192, 16),
                                                 (5, 6, 3)])
 def test_softmax_matches_oracle(fam, oracle_lib, rows, extent, period):

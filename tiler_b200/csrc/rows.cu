@@ -133,6 +133,7 @@ struct RmsElem<false> {
   __device__ static uint4 pack(const float* o) {
     return make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3]));
   }
+  static constexpr bool kPackCanonicalizes = false;
 };
 template <>
 struct RmsElem<true> {
@@ -146,12 +147,20 @@ struct RmsElem<true> {
       o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
     }
   }
+  // RNE to bf16 two at a time (cvt.rn.bf16x2.f32: a to the upper half, b to
+  // the lower), then NaN halves set to the canonical 0x7fc0
   __device__ static uint4 pack(const float* o) {
     uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) w[i] = (uint32_t)f32_to_bf16(o[2 * i]) | ((uint32_t)f32_to_bf16(o[2 * i + 1]) << 16);
+    for (int i = 0; i < 4; ++i) {
+      uint32_t p;
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(o[2 * i + 1]), "f"(o[2 * i]));
+      const uint32_t nan_halves = __vcmpgtu2(p & 0x7fff7fffu, 0x7f807f80u);
+      w[i] = (p & ~nan_halves) | (0x7fc07fc0u & nan_halves);
+    }
     return make_uint4(w[0], w[1], w[2], w[3]);
   }
+  static constexpr bool kPackCanonicalizes = true;
 };
 
 __device__ __forceinline__ uint4 ld_u4_policy(const void* p, uint64_t policy) {
@@ -166,6 +175,15 @@ __device__ __forceinline__ uint4 ld_u4_policy(const void* p, uint64_t policy) {
 // Software-pipelined: the shared-memory loads of batch k + 1 are issued
 // before the adds of batch k, so the dependent add chain never waits on a
 // load's latency (the warp issues in order).
+// Two binary32 squares with one mul.rn.f32x2 (each lane an IEEE RN product,
+// the same bits as two mul.rn.f32).
+__device__ __forceinline__ void square2(float a, float b, float& ra, float& rb) {
+  uint64_t in, out;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(in) : "f"(a), "f"(b));
+  asm("mul.rn.f32x2 %0, %1, %1;" : "=l"(out) : "l"(in));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(ra), "=f"(rb) : "l"(out));
+}
+
 template <class E>
 __device__ __forceinline__ void rms_fold_batch(float& acc, const uint4 (&q)[8]) {
 #pragma unroll
@@ -173,7 +191,12 @@ __device__ __forceinline__ void rms_fold_batch(float& acc, const uint4 (&q)[8]) 
     float e[E::kPerVec];
     E::unpack(q[b], e);
 #pragma unroll
-    for (int j = 0; j < E::kPerVec; ++j) acc = __fadd_rn(acc, __fmul_rn(e[j], e[j]));
+    for (int j = 0; j < E::kPerVec; j += 2) {
+      float s0, s1;
+      square2(e[j], e[j + 1], s0, s1);
+      acc = __fadd_rn(acc, s0);
+      acc = __fadd_rn(acc, s1);
+    }
   }
 }
 template <class E>
@@ -379,7 +402,11 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
               E::unpack(xv[u], xe);
               E::unpack(wq, we);
 #pragma unroll
-              for (int j = 0; j < E::kPerVec; ++j) ye[j] = canon(__fmul_rn(we[j], __fmul_rn(xe[j], s)));
+              for (int j = 0; j < E::kPerVec; ++j) {
+                // bf16 output: the packing maps every NaN to the canonical one
+                const float yv = __fmul_rn(we[j], __fmul_rn(xe[j], s));
+                ye[j] = E::kPackCanonicalizes ? yv : canon(yv);
+              }
               st_global_stream_u4(reinterpret_cast<uint4*>(yr + v * 16), E::pack(ye));
             }
           }
