@@ -92,7 +92,10 @@ struct RmsPipeSmem {
   float scale[2][kRmsWave];
 };
 // The broadcast weight row is staged once per CTA when it fits.
-constexpr int kRmsWeightBytes = 16384;
+#ifndef TILER_RMS_W_STAGE
+#define TILER_RMS_W_STAGE 1
+#endif
+constexpr int kRmsWeightBytes = TILER_RMS_W_STAGE ? 16384 : 16;
 #ifndef TILER_RMS_NORM_U
 #define TILER_RMS_NORM_U 8
 #endif
@@ -169,6 +172,18 @@ __device__ __forceinline__ uint4 ld_u4_policy(const void* p, uint64_t policy) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p), "l"(policy));
   return v;
+}
+
+// 32-byte global load (with an L2 policy) and streaming store, sm_100.
+__device__ __forceinline__ void ld_v8_policy(const void* p, uint64_t policy, uint4& a, uint4& b) {
+  asm volatile("ld.global.L2::cache_hint.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], %9;"
+               : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+               : "l"(p), "l"(policy));
+}
+__device__ __forceinline__ void st_v8_stream(void* p, const uint4& a, const uint4& b) {
+  asm volatile("st.global.cs.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(a.x), "r"(a.y), "r"(a.z),
+               "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
 }
 
 // Folds `n` 16-byte vectors of one staged row into acc (strict order).
@@ -371,6 +386,7 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
     // ---- normalize warps: y = w * (x * s), two roundings (rms_norm.rs:479-485)
     const uint32_t nw = pwarp - kRmsLoadWarps - 1;
     const uint64_t drop = policy_evict_first();
+    const bool wide = (uintptr_t)x % 32 == 0 && (uintptr_t)y % 32 == 0 && row_bytes % 32 == 0;
     const uint64_t nvec = row_bytes / 16;
     for (uint64_t wv = 0; wv < nwaves; ++wv) {
       const uint32_t wr = wave_rows_of(wv);
@@ -384,6 +400,39 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
         const uint8_t* xr = x + row * row_bytes;
         const uint8_t* wrow = w + (int64_t)row * w_row_stride * (int64_t)esize;
         uint8_t* yr = y + row * row_bytes;
+        auto norm_vec = [&](const uint4& xq, uint64_t v) {  // y for the 16-byte vector v of the row
+          const uint4 wq = w_staged ? reinterpret_cast<const uint4*>(SS.wrow)[v]
+                                    : __ldg(reinterpret_cast<const uint4*>(wrow + v * 16));
+          float xe[E::kPerVec], we[E::kPerVec], ye[E::kPerVec];
+          E::unpack(xq, xe);
+          E::unpack(wq, we);
+#pragma unroll
+          for (int j = 0; j < E::kPerVec; ++j) {
+            // bf16 output: the packing maps every NaN to the canonical one
+            const float yv = __fmul_rn(we[j], __fmul_rn(xe[j], s));
+            ye[j] = E::kPackCanonicalizes ? yv : canon(yv);
+          }
+          return E::pack(ye);
+        };
+        if (wide) {
+          // 32-byte loads and stores (half the memory instructions)
+          constexpr int U2 = TILER_RMS_NORM_U / 2;
+          const uint64_t npair = nvec / 2;
+          for (uint64_t p0 = lane; p0 < npair; p0 += 32 * U2) {
+            uint4 xa[U2], xb[U2];
+#pragma unroll
+            for (int u = 0; u < U2; ++u) {
+              const uint64_t pp = p0 + 32 * u;
+              if (pp < npair) ld_v8_policy(xr + pp * 32, drop, xa[u], xb[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < U2; ++u) {
+              const uint64_t pp = p0 + 32 * u;
+              if (pp < npair) st_v8_stream(yr + pp * 32, norm_vec(xa[u], 2 * pp), norm_vec(xb[u], 2 * pp + 1));
+            }
+          }
+          continue;
+        }
         constexpr int U = TILER_RMS_NORM_U;  // 16-byte loads of x in flight per lane
         for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * U) {
           uint4 xv[U];
@@ -395,20 +444,7 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
 #pragma unroll
           for (int u = 0; u < U; ++u) {
             const uint64_t v = v0 + 32 * u;
-            if (v < nvec) {
-              const uint4 wq = w_staged ? reinterpret_cast<const uint4*>(SS.wrow)[v]
-                                        : __ldg(reinterpret_cast<const uint4*>(wrow + v * 16));
-              float xe[E::kPerVec], we[E::kPerVec], ye[E::kPerVec];
-              E::unpack(xv[u], xe);
-              E::unpack(wq, we);
-#pragma unroll
-              for (int j = 0; j < E::kPerVec; ++j) {
-                // bf16 output: the packing maps every NaN to the canonical one
-                const float yv = __fmul_rn(we[j], __fmul_rn(xe[j], s));
-                ye[j] = E::kPackCanonicalizes ? yv : canon(yv);
-              }
-              st_global_stream_u4(reinterpret_cast<uint4*>(yr + v * 16), E::pack(ye));
-            }
+            if (v < nvec) st_global_stream_u4(reinterpret_cast<uint4*>(yr + v * 16), norm_vec(xv[u], v));
           }
         }
       }
