@@ -275,11 +275,14 @@ __device__ __forceinline__ uint32_t exp_cr_bits(float x, const double* table_hi,
   const double p = __fma_rn(__dmul_rn(r, r), q, r);
   const double tj = table_hi[n & 255];
   const double y0 = __fma_rn(tj, p, tj);
-  const int hi = __double2hiint(y0) + ((n >> 8) << 20);
+  const uint32_t hi = (uint32_t)__double2hiint(y0) + ((uint32_t)(n >> 8) << 20);
   const uint32_t lo = (uint32_t)__double2loint(y0);
-  const int d = (int)(lo & 0x1fffffffu) - 0x10000000;
-  *ok = hi >= 0x38100000 && hi < 0x47f00000 && (d > 64 || d < -64);
-  return ((uint32_t)(hi - 0x38000000) << 3) + (lo >> 29) + ((lo >> 28) & 1u);
+  // normal binary32 range: hi in [0x38100000, 0x47f00000); not within 64
+  // units of the midpoint pattern 1 << 28 in the low 29 bits
+  *ok = (hi - 0x38100000u) < (0x47f00000u - 0x38100000u) &&
+        ((lo & 0x1fffffffu) - (0x10000000u - 64u)) > 128u;
+  // binary32 bits: exponent rebased, 23 mantissa bits from hi:lo, rounded by bit 28
+  return __funnelshift_l(lo, hi - 0x38000000u, 3) + ((lo >> 28) & 1u);
 }
 
 // Correctly rounded binary32 1/sqrt(t) (certified_rsqrt_strict,
