@@ -547,6 +547,9 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
 #ifndef TILER_SMX_MAX_GROUP
 #define TILER_SMX_MAX_GROUP 6
 #endif
+#ifndef TILER_SMX_EXP_VECS
+#define TILER_SMX_EXP_VECS 1
+#endif
 constexpr int kSmxMaxGroup = TILER_SMX_MAX_GROUP;  // rows per CTA group
 constexpr uint64_t kSmxMaxExtent = 8192;
 
@@ -646,12 +649,18 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
         const float sh = __fsub_rn(xv, m);
         return sh > -104.0f ? exp_cr_fast(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
       };
-      for (uint32_t v = lane; v < live4; v += 32) {  // four independent exps per lane
-        const float4 q = b4[v];
-        const float xs[4] = {q.x, q.y, q.z, q.w};
-        uint32_t e[4], flagged = 0;
+      constexpr int EV = TILER_SMX_EXP_VECS;  // float4s per lane per step: 4 * EV independent exps
+      for (uint32_t v0 = lane; v0 < live4; v0 += 32 * EV) {
+        float xs[4 * EV];
+        uint32_t e[4 * EV], flagged = 0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int h = 0; h < EV; ++h) {
+          const uint32_t v = v0 + 32 * h;
+          const float4 q = v < live4 ? b4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+          xs[4 * h] = q.x; xs[4 * h + 1] = q.y; xs[4 * h + 2] = q.z; xs[4 * h + 3] = q.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4 * EV; ++i) {
           const float sh = __fsub_rn(xs[i], m);
           bool ok;
           e[i] = exp_cr_bits(sh, table, &ok);
@@ -659,10 +668,16 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
         }
         if (__any_sync(__activemask(), flagged != 0)) {  // rare: certify or special-case the flagged ones
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
+          for (int i = 0; i < 4 * EV; ++i)
             if ((flagged >> i) & 1u) e[i] = __float_as_uint(softmax_exp_slow(__fsub_rn(xs[i], m), table, st));
         }
-        b4[v] = make_float4(__uint_as_float(e[0]), __uint_as_float(e[1]), __uint_as_float(e[2]), __uint_as_float(e[3]));
+#pragma unroll
+        for (int h = 0; h < EV; ++h) {
+          const uint32_t v = v0 + 32 * h;
+          if (v < live4)
+            b4[v] = make_float4(__uint_as_float(e[4 * h]), __uint_as_float(e[4 * h + 1]), __uint_as_float(e[4 * h + 2]),
+                                __uint_as_float(e[4 * h + 3]));
+        }
       }
       for (uint32_t c = live4 * 4 + lane; c < live; c += 32) b[c] = exp_of(b[c]);
       for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) b[c] = 0.0f;
