@@ -43,21 +43,27 @@ __device__ __forceinline__ float butterfly(float v) {
 // Folds one sequence seq[0, n) under the composition (T = blockDim.x, k, R)
 // and returns the result in thread 0 (unCanonicalized).  `slots` is
 // shared scratch of R*G floats plus R floats.  All threads must call it.
+#ifndef TILER_SUM_CHUNK_ROUNDS
+#define TILER_SUM_CHUNK_ROUNDS 4
+#endif
+
 template <int OP, int K>
 __device__ float compose_block(const float* __restrict__ seq, uint64_t n, uint32_t R, float* slots,
                                bool vec_ok) {
   const uint32_t T = blockDim.x, G = T >> 5, tid = threadIdx.x;
   const uint32_t warp = tid >> 5, lane = tid & 31;
   const float ident = identity_value<OP>();
-  constexpr uint32_t CH = 8;  // rounds whose loads are in flight together
-  for (uint32_t r0 = 0; r0 < R; r0 += CH) {
-    float vals[CH][K];
+  // Software-pipelined in chunks of CH rounds: the loads of chunk c + 1 are
+  // issued before the folds of chunk c, so no chunk waits on a full memory
+  // latency after the previous one's arithmetic.
+  constexpr uint32_t CH = TILER_SUM_CHUNK_ROUNDS;
+  auto load_chunk = [&](uint32_t r0, float (&vals)[CH][K]) {
 #pragma unroll
     for (uint32_t c = 0; c < CH; ++c) {
-      uint64_t base = ((uint64_t)(r0 + c) * T + tid) * K;
+      const uint64_t base = ((uint64_t)(r0 + c) * T + tid) * K;
       if constexpr (K == 4) {
         if (r0 + c < R && base + K <= n && vec_ok) {
-          float4 v = __ldcs(reinterpret_cast<const float4*>(seq + base));
+          const float4 v = __ldcs(reinterpret_cast<const float4*>(seq + base));
           vals[c][0] = v.x; vals[c][1] = v.y; vals[c][2] = v.z; vals[c][3] = v.w;
           continue;
         }
@@ -65,6 +71,8 @@ __device__ float compose_block(const float* __restrict__ seq, uint64_t n, uint32
 #pragma unroll
       for (int i = 0; i < K; ++i) vals[c][i] = (r0 + c < R && base + i < n) ? __ldcs(seq + base + i) : ident;
     }
+  };
+  auto fold_chunk = [&](uint32_t r0, const float (&vals)[CH][K]) {
 #pragma unroll
     for (uint32_t c = 0; c < CH; ++c) {
       if (r0 + c >= R) break;
@@ -74,6 +82,16 @@ __device__ float compose_block(const float* __restrict__ seq, uint64_t n, uint32
       v = butterfly<OP>(v);
       if (lane == 0) slots[(r0 + c) * G + warp] = v;
     }
+  };
+  float cur[CH][K], nxt[CH][K];
+  load_chunk(0, cur);
+  for (uint32_t r0 = 0; r0 < R; r0 += CH) {
+    if (r0 + CH < R) load_chunk(r0 + CH, nxt);
+    fold_chunk(r0, cur);
+#pragma unroll
+    for (uint32_t c = 0; c < CH; ++c)
+#pragma unroll
+      for (int i = 0; i < K; ++i) cur[c][i] = nxt[c][i];
   }
   __syncthreads();
   float* staged = slots + R * G;
