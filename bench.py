@@ -281,6 +281,14 @@ def family_suite(fam, torch, world, steps_small, warmup):
     yq = torch.empty(16384, 4096, device=dev)
     cd = torch.empty_like(codes)
 
+    # fused RMS norm -> int8 quantize over the RMS config (x read once, y never written)
+    xr = torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=gen)
+    wr_ = torch.rand(RMS_EXTENT, device=dev, generator=gen) + 0.5
+    ms = time_device(lambda i: fam.rms_norm_quantize_i8(xr, wr_, check=False), steps_small, warmup, world)
+    rec("rms_norm_quantize_i8_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 5 + RMS_EXTENT * 4 + RMS_ROWS * 4, ms,
+        steps_small, hbm)
+    del xr
+
     def run_dec(i):
         L.tiler_cuda_dequantize_i8_rows(ctx, stream, None, codes.data_ptr(), scales.data_ptr(), 16384, 4096,
                                         yq.data_ptr())

@@ -242,6 +242,16 @@ int32_t tiler_cuda_softmax_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda
 int32_t tiler_cuda_quantize_i8_rows(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
                                     const float* x, uint64_t rows, uint64_t extent, int8_t* codes,
                                     float* scales);
+/* Fused RMS norm -> per-row int8 quantize (the "RMS norm -> quantize, one HBM
+ * read" fusion): codes/scales equal tiler_cuda_quantize_i8_rows applied to
+ * the y of tiler_cuda_rms_norm_f32 (rms_norm.rs:453-489, then
+ * quantization.rs:188-247, :404-430), bit for bit, with the same refusals
+ * (NaN y -> NAN_INPUT at its first column, scale not positive-normal ->
+ * SCALE_DOMAIN); y itself is never written.  x, w 16-byte aligned, extent a
+ * multiple of 4 (else UNSUPPORTED). */
+int32_t tiler_cuda_rms_norm_quantize_i8(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                        const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
+                                        uint64_t extent, uint32_t eps_bits, int8_t* codes, float* scales);
 /* dequantize_one (quantization.rs:440-451) with zero point 0, per-row scale.
  * Decoding cannot fail on any input; `status` (nullable) only counts bounded
  * waits of the staged kernel that ran out (TILER_CUDA_TIMEOUT). */

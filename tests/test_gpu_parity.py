@@ -329,6 +329,39 @@ def test_quantize_decode_match_oracle(fam, oracle_lib, rows, extent):
     assert_bits_equal(y, wy)
 
 
+@pytest.mark.parametrize("rows,extent,full_w", [(8192, 4096, False), (37, 1024, True), (300, 16, False)])
+def test_rms_norm_quantize_fusion_matches_the_composed_oracle(fam, oracle_lib, rows, extent, full_w):
+    # the fused family equals quantize_i8_rows(rms_norm_f32(x, w)) bit for bit
+    x = seeded_normal(rows + 7, rows * extent).reshape(rows, extent)
+    w = seeded_uniform(5, rows * extent if full_w else extent, 0.5, 1.5)
+    w = w.reshape(rows, extent) if full_w else w
+    codes, scales = fam.rms_norm_quantize_i8(cuda(x), cuda(w))
+    st, y = oracle_lib.rms_norm_f32(x, w, nthreads=8)
+    assert st == 0
+    st, wc, ws, _ = oracle_lib.quantize_i8_rows(y, nthreads=8)
+    assert st == 0
+    assert (host(codes) == wc).all()
+    assert_bits_equal(host(scales), ws)
+
+
+def test_rms_norm_quantize_fusion_refusals(fam):
+    extent = 256
+    x = seeded_normal(9, 4 * extent).reshape(4, extent)
+    w = np.ones(extent, np.float32)
+    bad = x.copy()
+    bad[2, 100] = np.nan  # the whole y row is NaN: its first column is reported
+    with pytest.raises(fam.TilerCudaError) as e:
+        fam.rms_norm_quantize_i8(cuda(bad), cuda(w))
+    assert e.value.code == 4 and e.value.position == 2 * extent
+    zero = x.copy()
+    zero[1, :] = 0.0  # y = 0: the scale is +0, not positive-normal
+    with pytest.raises(fam.TilerCudaError) as e:
+        fam.rms_norm_quantize_i8(cuda(zero), cuda(w))
+    assert e.value.code == 9 and e.value.position == 1 * extent
+    with pytest.raises(fam.TilerCudaError):  # extent not a multiple of 4
+        fam.rms_norm_quantize_i8(cuda(x[:, :255].copy()), cuda(w[:255].copy()))
+
+
 def test_quantize_half_integer_ties_are_exact(fam, oracle_lib):
     # rows whose quotients land on k + 0.5 exactly and within an ulp of it
     s = np.float32(127.0) / np.float32(127.0)

@@ -215,6 +215,8 @@ def _default_executor(symbol: str):
                                                                            a["per_partition"], a["rounds"],
                                                                            a.get("participant_major", False)),
         "tiler_cuda.quantize_i8_rows": lambda a: F.quantize_i8_rows(a["x"]),
+        "tiler_cuda.rms_norm_quantize_i8": lambda a: F.rms_norm_quantize_i8(a["x"], a["w"],
+                                                                             a.get("eps_bits", F.EPS_1E6_BITS)),
         "tiler_cuda.dequantize_i8_rows": lambda a: F.dequantize_i8_rows(a["codes"], a["scales"]),
         "tiler_cuda.quantize_affine_u8": lambda a: F.quantize_affine_u8(a["x"], a["scale"], a["zero_point"],
                                                                          a.get("maximum", 255)),

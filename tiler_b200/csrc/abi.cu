@@ -117,6 +117,7 @@ const Entry kEntries[] = {
     {"tiler_cuda.rms_norm_bf16", (const void*)rms_norm_kernel<true>, kRmsThreads, kRmsSmemBytes},
     {"tiler_cuda.softmax_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.quantize_i8_rows", (const void*)quantize_i8_rows_kernel, kQThreads, 0},
+    {"tiler_cuda.rms_norm_quantize_i8", (const void*)rms_norm_kernel<false, true>, kRmsThreads, kRmsSmemBytes},
     {"tiler_cuda.dequantize_i8_rows", (const void*)dequantize_i8_rows_kernel, 256, 0},
     {"tiler_cuda.quantize_affine_u8", (const void*)quantize_affine_u8_kernel, 256, 0},
     {"tiler_cuda.dequantize_affine_u8", (const void*)dequantize_affine_u8_kernel, 256, 0},
@@ -522,6 +523,24 @@ int32_t tiler_cuda_quantize_i8_rows(tiler_cuda_context* ctx, void* stream, tiler
   if (rows == 0) return TILER_CUDA_OK;
   if (!x || !codes || !scales || rows > 0x7fffffffull) return TILER_CUDA_INVALID_APPLICATION;
   launch_quantize_i8_rows(x, rows, extent, codes, scales, st, ctx->facts.sm_count, S(stream));
+  return last_error_status();
+}
+
+int32_t tiler_cuda_rms_norm_quantize_i8(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st, const float* x,
+                                        const float* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,
+                                        uint32_t eps_bits, int8_t* codes, float* scales) {
+  CHECK_CTX(ctx);
+  if (!eps_admitted(eps_bits) || w_row_stride < 0) return TILER_CUDA_INVALID_APPLICATION;
+  if (extent > (1ull << 24)) return TILER_CUDA_SHAPE_TOO_LARGE;
+  if (extent == 0) return TILER_CUDA_INVALID_APPLICATION;  // quantize has no empty row
+  if (rows == 0) return TILER_CUDA_OK;
+  if (!x || !w || !codes || !scales || rows > 0x7fffffffull) return TILER_CUDA_INVALID_APPLICATION;
+  if (w_row_stride != 0 && (uint64_t)w_row_stride != extent) return TILER_CUDA_UNSUPPORTED;
+  float eps;
+  memcpy(&eps, &eps_bits, 4);
+  const int r = launch_rms_norm_quantize_i8(x, w, w_row_stride, rows, extent, eps, codes, scales, st,
+                                            ctx->facts.sm_count, S(stream));
+  if (r != 0) return r;
   return last_error_status();
 }
 

@@ -30,6 +30,11 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
                     float eps, void* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream);
 int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t causal_period, uint64_t row_offset,
                    float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream);
+// Fused RMS norm (f32) -> per-row int8 quantize of y; TILER_CUDA_UNSUPPORTED for
+// unaligned operands or an extent that is not a multiple of 4.
+int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
+                                uint64_t extent, float eps, int8_t* codes, float* scales, tiler_cuda_status* st,
+                                int sm_count, cudaStream_t stream);
 void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
                              tiler_cuda_status* st, int sm_count, cudaStream_t stream);
 void launch_dequantize_i8_rows(const int8_t* codes, const float* scales, uint64_t rows, uint64_t extent, float* y,

@@ -240,11 +240,16 @@ __device__ __forceinline__ float rms_fold_vectors(float acc, uint32_t rowp, uint
   return acc;
 }
 
-template <bool BF16>
+__device__ __forceinline__ int code_of_bounded(float xv, float scale, float inv);
+
+// QUANT: the fused RMS norm -> per-row int8 quantize (f32 only): instead of
+// writing y, each normalize warp forms its row's y twice from the L2-resident
+// x (max|y| first, then the codes), so y never reaches HBM.
+template <bool BF16, bool QUANT = false>
 __global__ void __launch_bounds__(kRmsThreads, 1)
     rms_norm_kernel(const uint8_t* __restrict__ x, const uint8_t* __restrict__ w, int64_t w_row_stride,
                     uint64_t rows, uint64_t extent, float eps, uint8_t* __restrict__ y, uint32_t wave_rows,
-                    tiler_cuda_status* st) {
+                    tiler_cuda_status* st, int8_t* __restrict__ codes = nullptr, float* __restrict__ scales = nullptr) {
   using E = RmsElem<BF16>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   RmsSmem& SS = *reinterpret_cast<RmsSmem*>(smem_raw);
@@ -414,6 +419,66 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
           }
           return E::pack(ye);
         };
+        if constexpr (QUANT) {
+          // quantize_i8_rows of this row's y (quantization.rs:188-247, :404-430 with the
+          // per-row scale max|y| / 127): max over the magnitude bits, then the codes
+          constexpr int UQ = TILER_RMS_NORM_U;
+          uint32_t mb = 0;
+          for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * UQ) {
+            uint4 xv[UQ];
+#pragma unroll
+            for (int u = 0; u < UQ; ++u)
+              if (v0 + 32 * u < nvec) xv[u] = ld_u4_policy(xr + (v0 + 32 * u) * 16, drop);
+#pragma unroll
+            for (int u = 0; u < UQ; ++u)
+              if (v0 + 32 * u < nvec) {
+                const uint4 q = norm_vec(xv[u], v0 + 32 * u);
+                mb = max(mb, max(max(q.x & 0x7fffffffu, q.y & 0x7fffffffu), max(q.z & 0x7fffffffu, q.w & 0x7fffffffu)));
+              }
+          }
+          mb = __reduce_max_sync(0xffffffffu, mb);
+          if (mb > 0x7f800000u) {  // a NaN y: report its first column
+            uint32_t first = 0xffffffffu;
+            for (uint64_t v = lane; v < nvec; v += 32) {
+              const uint4 q = norm_vec(ld_u4_policy(xr + v * 16, drop), v);
+              const uint32_t b[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                if ((b[j] & 0x7fffffffu) > 0x7f800000u) first = min(first, (uint32_t)(v * 4 + j));
+            }
+            first = __reduce_min_sync(0xffffffffu, first);
+            if (lane == 0) report_error(st, row * extent + first, TILER_CUDA_NAN_INPUT);
+            continue;
+          }
+          const float scale = __fdiv_rn(__uint_as_float(mb), 127.0f);
+          if (lane == 0) scales[row] = scale;
+          if (!is_positive_normal(scale)) {
+            if (lane == 0) report_error(st, row * extent, TILER_CUDA_SCALE_DOMAIN);
+            continue;
+          }
+          const float inv = __frcp_rn(scale);
+          int* crow = reinterpret_cast<int*>(codes + row * extent);
+          for (uint64_t v0 = lane; v0 < nvec; v0 += 32 * UQ) {
+            uint4 xv[UQ];
+#pragma unroll
+            for (int u = 0; u < UQ; ++u)
+              if (v0 + 32 * u < nvec) xv[u] = ld_u4_policy(xr + (v0 + 32 * u) * 16, drop);
+#pragma unroll
+            for (int u = 0; u < UQ; ++u)
+              if (v0 + 32 * u < nvec) {
+                const uint4 q = norm_vec(xv[u], v0 + 32 * u);
+                const int c0 = code_of_bounded(__uint_as_float(q.x), scale, inv);
+                const int c1 = code_of_bounded(__uint_as_float(q.y), scale, inv);
+                const int c2 = code_of_bounded(__uint_as_float(q.z), scale, inv);
+                const int c3 = code_of_bounded(__uint_as_float(q.w), scale, inv);
+                uint32_t hi, packed;  // cvt.pack d, a, b, c: d = c << 16 | sat8(a) << 8 | sat8(b)
+                asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(c3), "r"(c2));
+                asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(packed) : "r"(c1), "r"(c0), "r"(hi));
+                __stcs(crow + v0 + 32 * u, (int)packed);
+              }
+          }
+          continue;
+        }
         if (wide) {
           // 32-byte loads and stores (half the memory instructions)
           constexpr int U2 = TILER_RMS_NORM_U / 2;
@@ -489,6 +554,21 @@ __global__ void rms_norm_generic_kernel(const void* __restrict__ xv, const void*
     const float v = canon(__fmul_rn(ld(w + (int64_t)row * w_row_stride, i), __fmul_rn(ld(x + row * extent, i), s)));
     if constexpr (BF16) y[row * extent + i] = f32_to_bf16(v); else y[row * extent + i] = v;
   }
+}
+
+int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
+                                uint64_t extent, float eps, int8_t* codes, float* scales, tiler_cuda_status* st,
+                                int sm_count, cudaStream_t stream) {
+  if (rows == 0 || extent == 0) return 0;
+  const bool aligned = ((uintptr_t)x % 16 == 0) && ((uintptr_t)w % 16 == 0) && ((uintptr_t)codes % 4 == 0) &&
+                       extent % 4 == 0;
+  if (!aligned) return TILER_CUDA_UNSUPPORTED;
+  const uint64_t grid = umin64((uint64_t)sm_count, rows);
+  cudaFuncSetAttribute(rms_norm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
+  rms_norm_kernel<false, true><<<(unsigned)grid, kRmsThreads, kRmsSmemBytes, stream>>>(
+      (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, nullptr, (uint32_t)kRmsWave, st, codes,
+      scales);
+  return 0;
 }
 
 int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,

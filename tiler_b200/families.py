@@ -224,6 +224,24 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, out
     return y
 
 
+def rms_norm_quantize_i8(x: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, check=True):
+    """Fused RMS norm -> per-row int8 quantize (f32): the codes and scales of
+    quantize_i8_rows(rms_norm(x, w)) without writing y."""
+    assert x.dtype == torch.float32 and w.dtype == torch.float32
+    extent = x.shape[-1]
+    rows = x.numel() // extent if extent else 0
+    stride = 0 if w.dim() == 1 else extent
+    codes = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    scales = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    st = _status() if check else None
+    _check(N.lib().tiler_cuda_rms_norm_quantize_i8(context(), _stream(), st.ptr if st else 0, _ptr(x), _ptr(w), stride,
+                                                   rows, extent, eps_bits, _ptr(codes), _ptr(scales)),
+           "rms_norm_quantize_i8")
+    if st:
+        _raise_from(st, "rms_norm_quantize_i8")
+    return codes, scales
+
+
 def rms_norm_host(x_host: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, out=None, x_dev=None,
                   y_dev=None, chunk_rows: int = 0, check=True) -> torch.Tensor:
     """RMS norm of host rows (tiler_cuda_rms_norm_host): chunked upload,
