@@ -270,6 +270,12 @@ def family_suite(fam, torch, world, steps_small, warmup):
     ysm = torch.empty_like(xsm)
     ms = time_device(lambda i: fam.softmax(xsm, causal_period=2048, out=ysm, check=False), steps_small, warmup, world)
     rec("softmax_f32_65536x2048_causal", "GB/s", 65536 * 2048 * 8, ms, steps_small, hbm)
+    # the same causal mask as a program tensor [2048, 2048] (0 / -inf), added in the kernel
+    col = torch.arange(2048, device=dev)
+    mask = torch.where(col[None, :] > col[:, None], float("-inf"), 0.0).contiguous()
+    ms = time_device(lambda i: fam.softmax_masked(xsm, mask, out=ysm, check=False), steps_small, warmup, world)
+    rec("softmax_masked_f32_65536x2048_mask_tensor", "GB/s", 65536 * 2048 * 8 + 2048 * 2048 * 4, ms, steps_small, hbm)
+    del mask
     del xsm, ysm
 
     # quantize / decode f32 [16384, 4096]

@@ -237,6 +237,17 @@ int32_t tiler_cuda_rms_norm_host(tiler_cuda_context* ctx, void* stream, tiler_cu
 int32_t tiler_cuda_softmax_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
                                const float* x, uint64_t rows, uint64_t extent,
                                uint64_t causal_period, uint64_t row_offset, float* y);
+/* Softmax of x + mask: the program's upstream add-f32 of a broadcast mask
+ * tensor (standard.rs:211-221) followed by SoftmaxF32Reference, fused: row r
+ * adds mask[(row_offset + r) mod mask_rows] (one rounding, NaN
+ * canonicalized) and takes the softmax of the sum.  mask is f32
+ * [mask_rows, extent] on the device.  With the block-causal 0 / -inf mask it
+ * equals tiler_cuda_softmax_f32 with causal_period = mask_rows bit for bit.
+ * Requires extent % 4 == 0, extent <= 8192, 16-byte aligned x, y, mask (else
+ * UNSUPPORTED). */
+int32_t tiler_cuda_softmax_masked_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                      const float* x, uint64_t rows, uint64_t extent, const float* mask,
+                                      uint64_t mask_rows, uint64_t row_offset, float* y);
 /* Strict-affine quantize, signed per-row extension of quantize
  * (quantization.rs:188-247, :404-430): scales[r] = max|x_r| / 127. */
 int32_t tiler_cuda_quantize_i8_rows(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,

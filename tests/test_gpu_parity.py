@@ -260,6 +260,38 @@ def test_softmax_matches_oracle(fam, oracle_lib, rows, extent, period):
     assert_bits_equal(got, want, f"softmax {rows}x{extent}")
 
 
+@pytest.mark.parametrize("rows,extent,mask_rows,row_offset", [(64, 2048, 64, 0), (100, 1000, 16, 5), (7, 8, 3, 2)])
+def test_softmax_with_a_mask_tensor_matches_oracle(fam, oracle_lib, rows, extent, mask_rows, row_offset):
+    # softmax(x + mask[(row_offset + r) mod mask_rows]): the add rounds once and
+    # canonicalizes NaN, then the reference softmax
+    x = seeded_normal(rows + 3, rows * extent).reshape(rows, extent) * 3
+    mask = seeded_normal(mask_rows + 1, mask_rows * extent).reshape(mask_rows, extent)
+    mask[seeded_uniform(6, mask_rows * extent, 0, 1).reshape(mask_rows, extent) < 0.3] = -np.inf
+    x[3 % rows, 1] = np.inf  # +inf + finite = +inf: that row's maximum is +inf
+    got = host(fam.softmax_masked(cuda(x), cuda(mask), row_offset=row_offset))
+    with np.errstate(invalid="ignore"):
+        t = x + mask[(row_offset + np.arange(rows)) % mask_rows]
+    t[np.isnan(t)] = np.array([0x7FC00000], np.uint32).view(np.float32)[0]
+    st, want = oracle_lib.softmax_f32(t, nthreads=8)
+    assert st == 0
+    assert_bits_equal(got, want, "masked softmax")
+
+
+def test_softmax_causal_mask_tensor_equals_the_in_kernel_mask(fam):
+    # the 0 / -inf block-causal mask as a tensor gives the in-kernel mask's bits,
+    # poisoned rows (NaN or +inf under the mask) included
+    rows, extent = 4096, 2048
+    gen = torch.Generator("cuda").manual_seed(21)
+    x = torch.randn(rows, extent, device="cuda", generator=gen) * 3
+    x[5, 2000] = float("nan")
+    x[6, 1999] = float("inf")
+    col = torch.arange(extent, device="cuda")
+    mask = torch.where(col[None, :] > torch.arange(extent, device="cuda")[:, None], float("-inf"), 0.0)
+    got = fam.softmax_masked(x, mask.contiguous())
+    want = fam.softmax(x, causal_period=extent)
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+
+
 def test_softmax_full_config_sampled_rows(fam, oracle_lib):
     rows, extent = 65536, 2048
     x = torch.randn(rows, extent, device="cuda", generator=torch.Generator("cuda").manual_seed(1)) * 3

@@ -206,6 +206,7 @@ def _default_executor(symbol: str):
         "tiler_cuda.rms_norm_f32": lambda a: F.rms_norm(a["x"], a["w"], a.get("eps_bits", F.EPS_1E6_BITS)),
         "tiler_cuda.rms_norm_bf16": lambda a: F.rms_norm(a["x"], a["w"], a.get("eps_bits", F.EPS_1E6_BITS)),
         "tiler_cuda.softmax_f32": lambda a: F.softmax(a["x"], a.get("causal_period", 0), a.get("row_offset", 0)),
+        "tiler_cuda.softmax_masked_f32": lambda a: F.softmax_masked(a["x"], a["mask"], a.get("row_offset", 0)),
         "tiler_cuda.sum_f32.grouped": lambda a: F.sum_f32(a["x"], a.get("grouping")),
         "tiler_cuda.max_f32.grouped": lambda a: F.max_f32(a["x"], a.get("grouping")),
         "tiler_cuda.sum_f32.strict": lambda a: F.strict_sum_f32(a["x"]),

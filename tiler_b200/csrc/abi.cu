@@ -118,6 +118,7 @@ const Entry kEntries[] = {
     {"tiler_cuda.softmax_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.quantize_i8_rows", (const void*)quantize_i8_rows_kernel, kQThreads, 0},
     {"tiler_cuda.rms_norm_quantize_i8", (const void*)rms_norm_kernel<false, true>, kRmsThreads, kRmsSmemBytes},
+    {"tiler_cuda.softmax_masked_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.dequantize_i8_rows", (const void*)dequantize_i8_rows_kernel, 256, 0},
     {"tiler_cuda.quantize_affine_u8", (const void*)quantize_affine_u8_kernel, 256, 0},
     {"tiler_cuda.dequantize_affine_u8", (const void*)dequantize_affine_u8_kernel, 256, 0},
@@ -513,6 +514,17 @@ int32_t tiler_cuda_softmax_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda
   if (rows == 0 || extent == 0) return TILER_CUDA_OK;
   if (!x || !y) return TILER_CUDA_INVALID_APPLICATION;
   launch_softmax(x, rows, extent, causal_period, row_offset, y, st, ctx->facts.sm_count, S(stream));
+  return last_error_status();
+}
+
+int32_t tiler_cuda_softmax_masked_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st, const float* x,
+                                      uint64_t rows, uint64_t extent, const float* mask, uint64_t mask_rows,
+                                      uint64_t row_offset, float* y) {
+  CHECK_CTX(ctx);
+  if (rows == 0 || extent == 0) return TILER_CUDA_OK;
+  if (!x || !y || !mask || mask_rows == 0) return TILER_CUDA_INVALID_APPLICATION;
+  const int r = launch_softmax(x, rows, extent, 0, row_offset, y, st, ctx->facts.sm_count, S(stream), mask, mask_rows);
+  if (r != 0) return r;
   return last_error_status();
 }
 

@@ -28,8 +28,13 @@ void launch_cooperative_sum(const float* x, uint64_t rows, uint64_t count, uint6
 // rows.cu
 int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,
                     float eps, void* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream);
+// mask (nullable): the additive mask tensor [mask_rows, extent] added to row r
+// as mask[(row_offset + r) mod mask_rows]; TILER_CUDA_UNSUPPORTED unless the
+// staged kernel applies (extent % 4 == 0, extent <= 8192, 16-byte aligned)
+// and causal_period == 0.
 int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t causal_period, uint64_t row_offset,
-                   float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream);
+                   float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream, const float* mask = nullptr,
+                   uint64_t mask_rows = 0);
 // Fused RMS norm (f32) -> per-row int8 quantize of y; TILER_CUDA_UNSUPPORTED for
 // unaligned operands or an extent that is not a multiple of 4.
 int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,

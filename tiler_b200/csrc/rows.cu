@@ -648,7 +648,8 @@ __device__ __noinline__ float softmax_exp_slow(float sh, const double* table, ti
 
 __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM)
     softmax_group_kernel(const float* __restrict__ x, uint64_t rows, uint64_t extent, uint64_t period,
-                         uint64_t row_offset, float* __restrict__ y, uint32_t group, tiler_cuda_status* st) {
+                         uint64_t row_offset, float* __restrict__ y, uint32_t group, tiler_cuda_status* st,
+                         const float* __restrict__ mask = nullptr, uint64_t mask_rows = 0) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   double* table = reinterpret_cast<double*>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + 2048);  // one per row buffer
@@ -708,9 +709,23 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
       float4* b4 = reinterpret_cast<float4*>(b);
       float m = __uint_as_float(0xff800000u);
       const uint32_t live4 = live / 4;
-      for (uint32_t v = lane; v < live4; v += 32) {
-        const float4 q = b4[v];
-        m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
+      if (mask) {
+        // the program's additive mask (an add-f32 of a broadcast mask tensor,
+        // standard.rs:211-221): t = x + mask[row mod mask_rows], one rounding,
+        // NaN canonicalized, written back in place before the maximum
+        const float4* m4 = reinterpret_cast<const float4*>(mask + ((row_offset + row) % mask_rows) * extent);
+        for (uint32_t v = lane; v < live4; v += 32) {
+          const float4 q = b4[v], a = __ldg(m4 + v);
+          const float4 t = make_float4(canon(__fadd_rn(q.x, a.x)), canon(__fadd_rn(q.y, a.y)),
+                                       canon(__fadd_rn(q.z, a.z)), canon(__fadd_rn(q.w, a.w)));
+          b4[v] = t;
+          m = max_nan(max_nan(m, t.x), max_nan(t.y, max_nan(t.z, t.w)));
+        }
+      } else {
+        for (uint32_t v = lane; v < live4; v += 32) {
+          const float4 q = b4[v];
+          m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
+        }
       }
       for (uint32_t c = live4 * 4 + lane; c < live; c += 32) m = max_nan(m, b[c]);
       uint32_t bad = 0;  // a masked x that is NaN or +inf poisons the row
@@ -899,7 +914,8 @@ __global__ void softmax_generic_kernel(const float* __restrict__ x, uint64_t row
 }
 
 int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t causal_period, uint64_t row_offset,
-                   float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+                   float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream, const float* mask,
+                   uint64_t mask_rows) {
   if (rows == 0 || extent == 0) return 0;
   // G rows per CTA, sized so three CTAs share an SM's shared memory.
   const size_t fixed = 2048 + 256, row_bytes = extent * 4;
@@ -908,6 +924,8 @@ int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t caus
   const uint64_t G = umin64(kSmxMaxGroup, umin64(rows, g3 >= 4 ? g3 : g1));
   const bool staged = (extent % 4 == 0) && extent <= kSmxMaxExtent && ((uintptr_t)x % 16 == 0) &&
                       ((uintptr_t)y % 16 == 0) && G >= 1;
+  if (mask && (!staged || causal_period != 0 || (uintptr_t)mask % 16 != 0 || mask_rows == 0))
+    return TILER_CUDA_UNSUPPORTED;  // the masked form runs on the staged kernel only
   if (!staged) {
     const unsigned wpb = 8;
     softmax_generic_kernel<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, 0, stream>>>(x, rows, extent,
@@ -921,7 +939,8 @@ int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t caus
   const int per_sm = std::max<int>(1, (int)((228 * 1024) / (smem + 1024)));
   const unsigned grid = (unsigned)umin64((rows + G - 1) / G, (uint64_t)sm_count * per_sm);
   softmax_group_kernel<<<grid, (unsigned)(32 * (G + 1)), smem, stream>>>(x, rows, extent, causal_period,
-                                                                          row_offset, y, (uint32_t)G, st);
+                                                                          row_offset, y, (uint32_t)G, st, mask,
+                                                                          mask_rows);
   return 0;
 }
 

@@ -224,6 +224,22 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, out
     return y
 
 
+def softmax_masked(x: torch.Tensor, mask: torch.Tensor, row_offset: int = 0, out=None, check=True) -> torch.Tensor:
+    """softmax(x + mask[(row_offset + r) mod mask_rows]) over the last axis:
+    the program's additive mask tensor fused into the softmax."""
+    assert x.dtype == torch.float32 and mask.dtype == torch.float32 and mask.shape[-1] == x.shape[-1]
+    extent = x.shape[-1]
+    rows = x.numel() // extent if extent else 0
+    mask_rows = mask.numel() // extent
+    y = torch.empty_like(x) if out is None else out
+    st = _status() if check else None
+    _check(N.lib().tiler_cuda_softmax_masked_f32(context(), _stream(), st.ptr if st else 0, _ptr(x), rows, extent,
+                                                 _ptr(mask), mask_rows, row_offset, _ptr(y)), "softmax_masked")
+    if st:
+        _raise_from(st, "softmax_masked")
+    return y
+
+
 def rms_norm_quantize_i8(x: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, check=True):
     """Fused RMS norm -> per-row int8 quantize (f32): the codes and scales of
     quantize_i8_rows(rms_norm(x, w)) without writing y."""
