@@ -606,20 +606,24 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
 // ---------------------------------------------------------------------------
 //
 // Each CTA owns G row buffers in shared memory (a buffer is one whole row)
-// and walks its block of rows in groups of G:
-//   1. one lane bulk-copies the group's rows in (one mbarrier);
-//   2. warp w takes row w: the row maximum over the unmasked columns
-//      (order-free, NaN-propagating), then e_i = exp(x_i - m) in place
-//      (certified exp); with the causal mask, columns past the diagonal
-//      hold e = +0 exactly (x + -inf = -inf), so they are zero-filled
-//      without evaluating exp, and a masked x that is NaN or +inf (which
-//      makes that e NaN) is recorded as a poisoned row;
+// and walks its groups of G consecutive rows:
+//   1. row warp w bulk-copies row w in (one mbarrier per row buffer), once
+//      its previous row's bulk store has read the buffer;
+//   2. warp w takes row w: with a mask tensor, t = x + mask first (in
+//      place); the row maximum over the unmasked columns (order-free,
+//      NaN-propagating), then e_i = exp(x_i - m) in place (certified exp,
+//      branch-free with one warp-uniform branch for flagged arguments); with
+//      the causal mask, columns past the diagonal hold e = +0 exactly
+//      (x + -inf = -inf), so they are zero-filled without evaluating exp,
+//      and a masked x that is NaN or +inf (which makes that e NaN) is
+//      recorded as a poisoned row;
 //   3. the chain warp folds all G denominators at once, lane w folding row
 //      w strictly, d = (((e_0 + e_1) + e_2) + ...), up to the diagonal only
 //      (adding +0.0 to a positive running sum is the identity), r = 1/d;
-//   4. warp w writes out_i = e_i * r with streaming stores.
-// Several CTAs share an SM (G is sized so three fit), so one CTA's loads
-// and folds overlap the others' exponentials and stores.
+//   4. warp w forms out_i = e_i * r in place over the live columns and
+//      writes the row back with one bulk store.
+// Four CTAs share an SM, so one CTA's loads and folds overlap the others'
+// exponentials and stores.
 
 #ifndef TILER_SMX_CTAS_PER_SM
 #define TILER_SMX_CTAS_PER_SM 4
