@@ -308,6 +308,28 @@ int32_t tiler_cuda_gemm_bf16(tiler_cuda_context* ctx, void* stream, tiler_cuda_s
                              const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k,
                              int32_t epilogue, uint16_t* c, uint64_t ldc);
 
+/* ---- multi-GPU: device buffers shared between the processes of one node ---- */
+/* cudaIpc handle (64 bytes) of the allocation holding `ptr`, and ptr's offset
+ * inside it. */
+int32_t tiler_cuda_ipc_export(tiler_cuda_context* ctx, const void* ptr, uint8_t* handle, uint64_t* offset);
+/* Maps a peer's exported buffer into this process: *out = base + offset. */
+int32_t tiler_cuda_ipc_open(tiler_cuda_context* ctx, const uint8_t* handle, uint64_t offset, void** out);
+int32_t tiler_cuda_ipc_close(tiler_cuda_context* ctx, void* ptr, uint64_t offset);
+/* The N-sharded contraction with its all-gather fused into the epilogue
+ * (the exchange step of the multi-GPU contraction; ncclAllGather is the
+ * unfused form): rank `rank` computes C_rank = A x B_shard^T ([m, n_shard],
+ * optional SiLU, bf16) and writes it into block `rank` of EVERY rank's block
+ * buffer [world, m, n_shard]: its own through TMA stores, the peers' with
+ * 16-byte stores over NVLink from the same staged boxes.  blocks[q] is rank
+ * q's buffer as mapped in this process (tiler_cuda_ipc_open for q != rank).
+ * The peers' blocks are complete once every rank's launch has completed:
+ * follow it with a collective on the same stream (e.g. a one-element
+ * all-reduce) before reading them.  world <= 8. */
+int32_t tiler_cuda_gemm_bf16_allgather(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                       const uint16_t* a, const uint16_t* b_shard, uint64_t m, uint64_t n_shard,
+                                       uint64_t k, int32_t epilogue, uint32_t rank, uint32_t world,
+                                       void* const* blocks);
+
 #ifdef __cplusplus
 }
 #endif

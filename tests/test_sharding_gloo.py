@@ -42,6 +42,31 @@ def _worker(rank, world, port, q):
         w = torch.from_numpy(rng.standard_normal((n, k)).astype(np.float32))
         c0, c1 = sharding.row_range(n, rank, world)
         c = sharding.gemm_n_sharded(a, w[c0:c1].contiguous(), lambda aa, ww: aa @ ww.t())
+
+        # the fused form's host logic: every rank's buffer mapped in rank order,
+        # the fused GEMM called with them, then the ordering collective
+        opened, closed, calls = [], [], []
+
+        def export(t):
+            return bytes([rank]) * 64, 16 * rank
+
+        def open_peer(handle, offset):
+            opened.append((handle[0], offset))
+            return 1000 + 10 * handle[0] + offset
+
+        blocks = sharding.PeerBlocks(torch.zeros(world, m, c1 - c0), export, open_peer,
+                                     lambda p, o: closed.append((p, o)))
+
+        def fused(aa, ww, ptrs, r, nw):
+            calls.append((list(ptrs), r, nw))
+            blocks.local[r] = aa @ ww.t()
+        got = sharding.gemm_n_sharded_fused(a, w[c0:c1].contiguous(), blocks, fused)
+        blocks.close()
+        peer = 1 - rank
+        assert opened == [(peer, 16 * peer)] and closed == [(1000 + 10 * peer + 16 * peer, 16 * peer)]
+        want_ptrs = [blocks.local.data_ptr() if q_ == rank else 1000 + 10 * q_ + 16 * q_ for q_ in range(world)]
+        assert calls == [(want_ptrs, rank, world)]
+        assert got is blocks.local and torch.equal(got[rank], a @ w[c0:c1].t())
         q.put((rank, np.float32(total).view(np.uint32).item(), c.numpy(), g))
     except Exception as exc:  # report instead of leaving the peer waiting
         q.put((rank, None, repr(exc), None))

@@ -657,4 +657,73 @@ int32_t tiler_cuda_gemm_bf16(tiler_cuda_context* ctx, void* stream, tiler_cuda_s
   return last_error_status();
 }
 
+// ---- device buffers shared between the processes of a node -------------------
+
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+int32_t tiler_cuda_ipc_export(tiler_cuda_context* ctx, const void* ptr, uint8_t* handle, uint64_t* offset) {
+  CHECK_CTX(ctx);
+  if (!ptr || !handle || !offset) return TILER_CUDA_INVALID_APPLICATION;
+  static AddressRangeFn range = nullptr;
+  if (!range) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return TILER_CUDA_DEVICE_ERROR;
+    range = (AddressRangeFn)p;
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, (CUdeviceptr)(uintptr_t)ptr) != CUDA_SUCCESS) return TILER_CUDA_INVALID_APPLICATION;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, (void*)(uintptr_t)base) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
+  memcpy(handle, &h, sizeof(h));
+  *offset = (uint64_t)((uintptr_t)ptr - (uintptr_t)base);
+  return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_ipc_open(tiler_cuda_context* ctx, const uint8_t* handle, uint64_t offset, void** out) {
+  CHECK_CTX(ctx);
+  if (!handle || !out) return TILER_CUDA_INVALID_APPLICATION;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
+  *out = (uint8_t*)base + offset;
+  return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_ipc_close(tiler_cuda_context* ctx, void* ptr, uint64_t offset) {
+  CHECK_CTX(ctx);
+  if (!ptr) return TILER_CUDA_INVALID_APPLICATION;
+  return cudaIpcCloseMemHandle((uint8_t*)ptr - offset) == cudaSuccess ? TILER_CUDA_OK : TILER_CUDA_DEVICE_ERROR;
+}
+
+int32_t tiler_cuda_gemm_bf16_allgather(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st,
+                                       const uint16_t* a, const uint16_t* b_shard, uint64_t m, uint64_t n_shard,
+                                       uint64_t k, int32_t epilogue, uint32_t rank, uint32_t world,
+                                       void* const* blocks) {
+  CHECK_CTX(ctx);
+  if (epilogue != 0 && epilogue != 1) return TILER_CUDA_INVALID_APPLICATION;
+  if (k == 0 || world == 0 || rank >= world || !blocks) return TILER_CUDA_INVALID_APPLICATION;
+  if (world > 8) return TILER_CUDA_UNSUPPORTED;
+  if (m == 0 || n_shard == 0) return TILER_CUDA_OK;
+  if (!a || !b_shard) return TILER_CUDA_INVALID_APPLICATION;
+  for (uint32_t q = 0; q < world; ++q)
+    if (!blocks[q]) return TILER_CUDA_INVALID_APPLICATION;
+  if (m / 128 * (n_shard / 256) > 0xffffffffull || k > (1ull << 31)) return TILER_CUDA_SHAPE_TOO_LARGE;
+  // block r of every buffer holds rank r's [m, n_shard] columns
+  const uint64_t block_elems = m * n_shard;
+  uint16_t* local = (uint16_t*)blocks[rank] + (uint64_t)rank * block_elems;
+  uint16_t* peer[8] = {};
+  uint32_t np = 0;
+  for (uint32_t q = 0; q < world; ++q)
+    if (q != rank) peer[np++] = (uint16_t*)blocks[q] + (uint64_t)rank * block_elems;
+  int32_t r = launch_gemm_bf16(a, b_shard, m, n_shard, k, epilogue, local, n_shard, st, ctx->facts.sm_count,
+                               S(stream), peer, np);
+  if (r != TILER_CUDA_OK) return r;
+  return last_error_status();
+}
+
 }  // extern "C"

@@ -71,6 +71,16 @@ constexpr int kGemmEpiWarps = 8;  // two per TMEM lane quarter, each draining ha
 constexpr int kGemmThreads = 32 * (2 + kGemmEpiWarps);
 constexpr uint32_t kTmemCols = 512;
 
+// All-gather fused into the epilogue: every output box of this rank is also
+// written into the same place of each peer's block buffer [world, m, n]
+// (rank-major blocks; block r holds rank r's columns), with plain 16-byte
+// stores over NVLink from the staged box.  The local copy goes out by TMA.
+constexpr int kGemmMaxPeers = 8;
+struct GemmPeers {
+  uint16_t* block[kGemmMaxPeers];  // this rank's block inside each rank's buffer (nullptr: skip)
+  uint32_t count;
+};
+
 // Epilogue staging: per epilogue warp one 32-row x 64-column bf16 box
 // (4 KB, 128-byte swizzle) that a TMA store writes to C.
 constexpr int kEpiBoxCols = 64;
@@ -131,7 +141,8 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                              const __grid_constant__ CUtensorMap tmap_c, uint32_t m_blocks, uint32_t n_blocks,
-                             uint32_t k_blocks, int epilogue, tiler_cuda_status* st) {
+                             uint32_t k_blocks, int epilogue, tiler_cuda_status* st,
+                             const __grid_constant__ GemmPeers peers, uint64_t ldp) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = ((raw + 1023) & ~1023u) - raw;
@@ -267,12 +278,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                        : "memory");
           asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
+        if (peers.count) {
+          // the box to each peer: 8 lanes per 128-byte row, 4 rows per step
+          const uint32_t c = lane & 7, rr = lane >> 3;
+          const uint64_t col = (uint64_t)nb * kBN + box + c * 8;
+#pragma unroll
+          for (uint32_t r0 = 0; r0 < 32; r0 += 4) {
+            const uint32_t r = r0 + rr;
+            const uint4 v = lds_u4(stage_u32 + r * 128 + ((c ^ (r & 7)) * 16));
+            const uint64_t row = (uint64_t)mb * kBM + quarter * 32 + r;
+            for (uint32_t q = 0; q < peers.count; ++q)
+              if (peers.block[q]) *reinterpret_cast<uint4*>(peers.block[q] + row * ldp + col) = v;
+          }
+        }
       }
       tmem_fence_before();
       mbar_arrive(&B.tmem_empty[buf]);
     }
     // the stores have completed before the CTA (and its shared memory) goes away
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (peers.count) __threadfence_system();  // the peer stores are visible before the kernel ends
   }
   tmem_fence_before();
   __syncthreads();
@@ -290,7 +315,15 @@ static bool make_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 }
 
 int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k, int epilogue,
-                     uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+                     uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream,
+                     uint16_t* const* peer_blocks, uint32_t npeers) {
+  if (npeers > (uint32_t)kGemmMaxPeers) return TILER_CUDA_UNSUPPORTED;
+  GemmPeers peers{};
+  peers.count = npeers;
+  for (uint32_t q = 0; q < npeers; ++q) {
+    peers.block[q] = peer_blocks[q];
+    if (peer_blocks[q] && (uintptr_t)peer_blocks[q] % 16) return TILER_CUDA_UNSUPPORTED;
+  }
   if (m % kBM || n % kBN || k % kBK || k == 0) return TILER_CUDA_UNSUPPORTED;
   if ((uintptr_t)a % 16 || (uintptr_t)b % 16 || (uintptr_t)c % 16 || ldc % 8 || ldc < n) return TILER_CUDA_UNSUPPORTED;
   CUtensorMap ta, tb, tcm;
@@ -303,7 +336,8 @@ int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t 
   const uint32_t tiles = mbk * nbk;
   const unsigned grid = std::min<uint32_t>(tiles, (uint32_t)sm_count);
   cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
-  gemm_bf16_tcgen05_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(ta, tb, tcm, mbk, nbk, kbk, epilogue, st);
+  gemm_bf16_tcgen05_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(ta, tb, tcm, mbk, nbk, kbk, epilogue, st, peers,
+                                                                      ldc);
   return TILER_CUDA_OK;
 }
 

@@ -61,8 +61,11 @@ void launch_status_reset(tiler_cuda_status* st, cudaStream_t stream);
 // gemm.cu
 void launch_contract_f32(const float* a, const float* b, uint64_t m, uint64_t n, uint64_t k, float* c,
                          cudaStream_t stream);
+// peer_blocks (nullable entries): where this rank's C also goes, one pointer per
+// rank (row pitch ldc); the all-gather fused into the epilogue.
 int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k, int epilogue,
-                     uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream);
+                     uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream,
+                     uint16_t* const* peer_blocks = nullptr, uint32_t npeers = 0);
 
 // Kernel registry (entry symbols for payload validation / entry queries).
 struct EntryInfo {

@@ -410,6 +410,45 @@ def contract_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return c
 
 
+def ipc_export(t: torch.Tensor):
+    """(64-byte cudaIpc handle, offset) of the device allocation holding t."""
+    handle = (C.c_uint8 * 64)()
+    offset = C.c_uint64(0)
+    _check(N.lib().tiler_cuda_ipc_export(context(), _ptr(t), handle, C.byref(offset)), "ipc_export")
+    return bytes(handle), offset.value
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """A peer's exported buffer mapped into this process (device pointer)."""
+    out = C.c_void_p()
+    h = (C.c_uint8 * 64).from_buffer_copy(handle)
+    _check(N.lib().tiler_cuda_ipc_open(context(), h, offset, C.byref(out)), "ipc_open")
+    return out.value
+
+
+def ipc_close(ptr: int, offset: int):
+    _check(N.lib().tiler_cuda_ipc_close(context(), ptr, offset), "ipc_close")
+
+
+def gemm_bf16_allgather(a: torch.Tensor, b_shard: torch.Tensor, blocks, rank: int, world: int,
+                        epilogue: str = "silu", check=True):
+    """The N-sharded contraction with the all-gather fused into the epilogue:
+    C_rank = A x B_shard^T goes into block `rank` of every rank's [world, m,
+    n_shard] buffer (``blocks``: each rank's buffer as a device pointer in this
+    process).  Complete on a peer once a later collective on the stream has
+    completed there."""
+    assert a.dtype == torch.bfloat16 and b_shard.dtype == torch.bfloat16 and len(blocks) == world
+    m, k = a.shape
+    n = b_shard.shape[0]
+    arr = (C.c_void_p * world)(*blocks)
+    st = _status() if check else None
+    _check(N.lib().tiler_cuda_gemm_bf16_allgather(context(), _stream(), st.ptr if st else 0, a.data_ptr(),
+                                                  b_shard.data_ptr(), m, n, k, 1 if epilogue == "silu" else 0,
+                                                  rank, world, arr), "gemm_bf16_allgather")
+    if st:
+        _raise_from(st, "gemm_bf16_allgather")
+
+
 def gemm_bf16(a: torch.Tensor, b: torch.Tensor, epilogue: str = "silu", out=None, check=True) -> torch.Tensor:
     """bf16 A[m,k] x B[n,k] on tcgen05 tensor cores, f32 accumulation,
     optional SiLU epilogue, bf16 output [m,n]."""

@@ -57,6 +57,50 @@ def sum_across_ranks(shard: torch.Tensor, local_sum, group=None) -> np.float32:
     return _strict_fold(gathered.cpu().numpy())
 
 
+class PeerBlocks:
+    """A [world, m, n] block buffer on every rank, each mapped into every
+    rank's process (the target of the fused GEMM + all-gather).  ``export``
+    and ``open_peer`` are the IPC calls (injected so the host logic runs
+    without a GPU in tests); ``ptrs[q]`` is rank q's buffer in this process."""
+
+    def __init__(self, local: torch.Tensor, export, open_peer, close_peer=None, group=None):
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        assert local.dim() == 3 and local.shape[0] == self.world
+        self.local = local
+        info = export(local)
+        infos = [None] * self.world
+        dist.all_gather_object(infos, info, group=group)
+        self._close = close_peer
+        self._opened = []
+        self.ptrs = []
+        for q, (handle, offset) in enumerate(infos):
+            if q == self.rank:
+                self.ptrs.append(local.data_ptr())
+            else:
+                p = open_peer(handle, offset)
+                self._opened.append((p, offset))
+                self.ptrs.append(p)
+
+    def close(self):
+        if self._close:
+            for p, offset in self._opened:
+                self._close(p, offset)
+        self._opened = []
+
+
+def gemm_n_sharded_fused(a: torch.Tensor, w_shard: torch.Tensor, blocks: PeerBlocks, fused_gemm, group=None):
+    """The contraction's multi-GPU form with the exchange fused into the GEMM:
+    ``fused_gemm(a, w_shard, ptrs, rank, world)`` writes this rank's columns
+    into every rank's block buffer; a one-element all-reduce on the stream then
+    orders every rank's kernel before anyone reads.  Returns the local
+    [world, m, n/world] blocks (the layout ``gemm_n_sharded(assemble=False)``
+    returns)."""
+    fused_gemm(a, w_shard, blocks.ptrs, blocks.rank, blocks.world)
+    done = torch.zeros(1, device=a.device)
+    dist.all_reduce(done, group=group)
+    return blocks.local
+
+
 def gemm_n_sharded(a: torch.Tensor, w_shard: torch.Tensor, local_gemm, group=None, assemble: bool = True):
     """C = local_gemm(a, w_shard) on every rank ([M, N/W] each), then one
     all-gather.  Returns [M, N] (assemble=True) or the rank-major blocks
