@@ -67,19 +67,36 @@ class PeerBlocks:
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         assert local.dim() == 3 and local.shape[0] == self.world
         self.local = local
-        info = export(local)
-        infos = [None] * self.world
-        dist.all_gather_object(infos, info, group=group)
         self._close = close_peer
         self._opened = []
         self.ptrs = []
-        for q, (handle, offset) in enumerate(infos):
-            if q == self.rank:
-                self.ptrs.append(local.data_ptr())
-            else:
-                p = open_peer(handle, offset)
-                self._opened.append((p, offset))
-                self.ptrs.append(p)
+        # every rank learns of a failure on any rank (no rank is left waiting
+        # in a collective the others skipped)
+        try:
+            info = export(local)
+        except Exception as exc:  # noqa: BLE001 - reported to every rank below
+            info = ("error", repr(exc))
+        infos = [None] * self.world
+        dist.all_gather_object(infos, info, group=group)
+        failed = [q for q, i in enumerate(infos) if i[0] == "error"]
+        error = None if not failed else f"export failed on rank {failed[0]}: {infos[failed[0]][1]}"
+        if error is None:
+            try:
+                for q, (handle, offset) in enumerate(infos):
+                    if q == self.rank:
+                        self.ptrs.append(local.data_ptr())
+                    else:
+                        p = open_peer(handle, offset)
+                        self._opened.append((p, offset))
+                        self.ptrs.append(p)
+            except Exception as exc:  # noqa: BLE001
+                error = f"open failed on rank {self.rank}: {exc!r}"
+        errors = [None] * self.world
+        dist.all_gather_object(errors, error, group=group)
+        bad = [e for e in errors if e]
+        if bad:
+            self.close()
+            raise RuntimeError(bad[0])
 
     def close(self):
         if self._close:
