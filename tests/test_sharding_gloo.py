@@ -67,6 +67,17 @@ def _worker(rank, world, port, q):
         want_ptrs = [blocks.local.data_ptr() if q_ == rank else 1000 + 10 * q_ + 16 * q_ for q_ in range(world)]
         assert calls == [(want_ptrs, rank, world)]
         assert got is blocks.local and torch.equal(got[rank], a @ w[c0:c1].t())
+
+        # a mapping failure on one rank is raised on every rank alike
+        def export_fails_on_1(t):
+            if rank == 1:
+                raise OSError("no IPC here")
+            return export(t)
+        try:
+            sharding.PeerBlocks(torch.zeros(world, 2, 2), export_fails_on_1, open_peer)
+            raise AssertionError("expected a RuntimeError")
+        except RuntimeError as exc:
+            assert "rank 1" in str(exc)
         q.put((rank, np.float32(total).view(np.uint32).item(), c.numpy(), g))
     except Exception as exc:  # report instead of leaving the peer waiting
         q.put((rank, None, repr(exc), None))
