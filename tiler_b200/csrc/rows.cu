@@ -42,9 +42,6 @@ namespace tc {
 //              stores, while the producer and the chain move on.  A broadcast
 //              weight row is staged in shared memory once per CTA.
 
-#ifndef TILER_RMS_BULK_LOAD
-#define TILER_RMS_BULK_LOAD 1
-#endif
 // pipeline p > 0 starts once pipeline p - 1 has folded NUM/DEN of its first wave
 #ifndef TILER_RMS_STAGGER_NUM
 #define TILER_RMS_STAGGER_NUM 1
@@ -72,7 +69,7 @@ constexpr int kRmsPitch = kRmsSlabBytes + 16;
 constexpr int kRmsWave = TILER_RMS_WAVE;  // rows per wave (one chain lane per row), <= 32
 constexpr int kRmsStages = TILER_RMS_STAGES;
 constexpr int kRmsPipes = TILER_RMS_PIPES;
-constexpr int kRmsLoadWarps = TILER_RMS_BULK_LOAD ? 1 : 2;
+constexpr int kRmsLoadWarps = 1;
 constexpr int kRmsNormWarps = TILER_RMS_NORM_WARPS;
 constexpr int kRmsPipeWarps = kRmsLoadWarps + 1 + kRmsNormWarps;
 // x is loaded with evict_last so it stays in L2 until the normalize pass
@@ -106,16 +103,6 @@ struct RmsSmem {
 };
 constexpr size_t kRmsSmemBytes = sizeof(RmsSmem);
 
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
-}
-__device__ __forceinline__ void cp_async16_hint(uint32_t saddr, const void* g, uint64_t policy) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(saddr), "l"(g), "l"(policy)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 // Shared-memory 16-byte load.  Volatile so the compiler cannot speculate it
 // above the lane predicate that keeps its address inside the allocation.
 __device__ __forceinline__ uint4 lds_u4_nv(uint32_t saddr) {
@@ -272,7 +259,7 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
   if (threadIdx.x == 0) {
     for (int p = 0; p < kRmsPipes; ++p) {
       RmsPipeSmem& Q = SS.pipe[p];
-      for (int s = 0; s < kRmsStages; ++s) { mbar_init(&Q.full[s], TILER_RMS_BULK_LOAD ? 1 : kRmsLoadWarps * 32); mbar_init(&Q.empty[s], 1); }
+      for (int s = 0; s < kRmsStages; ++s) { mbar_init(&Q.full[s], kRmsLoadWarps); mbar_init(&Q.empty[s], 1); }
       for (int s = 0; s < 2; ++s) { mbar_init(&Q.scale_full[s], 1); mbar_init(&Q.scale_empty[s], kRmsNormWarps); }
       mbar_init(&Q.started, 1);
     }
@@ -293,12 +280,10 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
 
   if (pwarp < kRmsLoadWarps) {
     // ---- producers -----------------------------------------------------------
-    const uint32_t t = pwarp * 32 + lane;
     // x stays in L2 until the normalize pass re-reads it (with evict_first)
     const uint64_t keep = TILER_RMS_KEEP_X ? policy_evict_last() : policy_evict_normal();
     if (pipe > 0 && !mbar_wait(&SS.pipe[pipe - 1].started, 0, st))
       *abort_flag = 1;
-#if TILER_RMS_BULK_LOAD
     // one warp: per stage, lane r issues one bulk copy of row r's slab
     // (padded pitch), completing on the stage's mbarrier
     if (pwarp == 0) {
@@ -315,28 +300,6 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
         if (lane < wr) bulk_g2s(&S.stage[stage][lane * kRmsPitch], gbase + lane * row_bytes, bytes, &S.full[stage], keep);
       }
     }
-#else
-    for (uint64_t i = 0; i < total && !*abort_flag; ++i) {
-      const uint32_t stage = i % kRmsStages;
-      const uint64_t use = i / kRmsStages;
-      if (use > 0 && !mbar_wait(&S.empty[stage], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
-      const uint64_t wv = i / nslabs, c = i % nslabs;
-      const uint32_t wr = wave_rows_of(wv);
-      const uint32_t chunks = (uint32_t)umin64(kRmsSlabBytes, row_bytes - c * kRmsSlabBytes) / 16;
-      const uint32_t sbase = smem_u32(&S.stage[stage][0]);
-      const uint8_t* gbase = x + (rb + wave_first_row(wv)) * row_bytes + c * kRmsSlabBytes;
-      for (uint32_t q = t; q < wr * (kRmsSlabBytes / 16); q += kRmsLoadWarps * 32) {
-        const uint32_t r = q / (kRmsSlabBytes / 16), c16 = q % (kRmsSlabBytes / 16);
-#if TILER_RMS_KEEP_X
-        if (c16 < chunks) cp_async16_hint(sbase + r * kRmsPitch + c16 * 16, gbase + r * row_bytes + c16 * 16, keep);
-#else
-        if (c16 < chunks) cp_async16(sbase + r * kRmsPitch + c16 * 16, gbase + r * row_bytes + c16 * 16);
-#endif
-      }
-      cp_async_arrive(&S.full[stage]);
-    }
-    asm volatile("cp.async.wait_all;" ::: "memory");
-#endif
 #ifdef TILER_RMS_PROBE_TL
     if (threadIdx.x == 0) tl[5] = global_ns();
 #endif
