@@ -308,6 +308,14 @@ int32_t tiler_cuda_gemm_bf16(tiler_cuda_context* ctx, void* stream, tiler_cuda_s
                              const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k,
                              int32_t epilogue, uint16_t* c, uint64_t ldc);
 
+/* Failure detection without a GPU fault: runs the bounded device wait every
+ * kernel uses on an mbarrier phase that nothing completes, with a limit of
+ * limit_ns (<= 2 s).  The wait gives up, counts a timeout in `status`
+ * (tiler_cuda_status_decode then reports TILER_CUDA_TIMEOUT) and the kernel
+ * returns with nothing in flight, so the context stays usable. */
+int32_t tiler_cuda_bounded_wait_selftest(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                         uint64_t limit_ns);
+
 /* ---- multi-GPU: device buffers shared between the processes of one node ---- */
 /* cudaIpc handle (64 bytes) of the allocation holding `ptr`, and ptr's offset
  * inside it. */

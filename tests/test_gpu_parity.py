@@ -4,6 +4,8 @@ work and for every family whose reference arithmetic the kernel restates;
 the bf16 contraction is held to the BASELINE tolerance (1e-2 relative)."""
 import hashlib
 
+import time
+
 import numpy as np
 import pytest
 
@@ -449,6 +451,25 @@ def test_quantize_staged_rows_refusals_and_extremes(fam, oracle_lib):
     with pytest.raises(fam.TilerCudaError) as e:
         fam.quantize_i8_rows(cuda(bad))
     assert e.value.code == 4 and e.value.position == 2 * 4096 + 3000
+
+
+def test_a_bounded_device_wait_that_runs_out_reports_a_timeout_and_the_context_stays_usable(fam, oracle_lib):
+    # the wait every kernel uses, on an mbarrier phase nothing completes, with a
+    # 20 ms limit: the status word reports TIMEOUT and later launches still work
+    from tiler_b200 import _native as N
+    st = fam.StatusWord()
+    st.reset()
+    t0 = time.monotonic()
+    assert N.lib().tiler_cuda_bounded_wait_selftest(fam.context(), torch.cuda.current_stream().cuda_stream,
+                                                    st.ptr, 20_000_000) == 0
+    torch.cuda.synchronize()
+    assert time.monotonic() - t0 < 5.0
+    assert st.fetch().code == N.TIMEOUT
+    x = seeded_normal(3, 8 * 64).reshape(8, 64)
+    w = np.ones(64, np.float32)
+    got = host(fam.rms_norm(cuda(x), cuda(w)))
+    _, want = oracle_lib.rms_norm_f32(x, w)
+    assert_bits_equal(got, want)
 
 
 def test_gather_full_config_is_bit_exact(fam):

@@ -96,6 +96,7 @@ SIGNATURES = {
     "tiler_cuda_rms_norm_host": (i32, [P, P, P, i32, P, P, P, i64, u64, u64, u32, P, P, u64]),
     "tiler_cuda_rms_norm_quantize_i8": (i32, [P, P, P, P, P, i64, u64, u64, u32, P, P]),
     "tiler_cuda_softmax_masked_f32": (i32, [P, P, P, P, u64, u64, P, u64, u64, P]),
+    "tiler_cuda_bounded_wait_selftest": (i32, [P, P, P, u64]),
     "tiler_cuda_ipc_export": (i32, [P, P, P, P]),
     "tiler_cuda_ipc_open": (i32, [P, P, u64, P]),
     "tiler_cuda_ipc_close": (i32, [P, P, u64]),

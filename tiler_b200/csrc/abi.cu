@@ -517,6 +517,14 @@ int32_t tiler_cuda_softmax_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda
   return last_error_status();
 }
 
+int32_t tiler_cuda_bounded_wait_selftest(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st,
+                                         uint64_t limit_ns) {
+  CHECK_CTX(ctx);
+  if (!st || limit_ns == 0 || limit_ns > kWaitLimitNs) return TILER_CUDA_INVALID_APPLICATION;
+  launch_bounded_wait_selftest(st, limit_ns, S(stream));
+  return last_error_status();
+}
+
 int32_t tiler_cuda_softmax_masked_f32(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st, const float* x,
                                       uint64_t rows, uint64_t extent, const float* mask, uint64_t mask_rows,
                                       uint64_t row_offset, float* y) {

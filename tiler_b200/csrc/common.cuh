@@ -436,12 +436,13 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, tiler_cuda_status* st) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, tiler_cuda_status* st,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    if ((i & 255) == 0 && global_ns() - t0 > limit_ns) break;
   }
   if (st) atomicAdd(&st->timeouts, 1u);
   return false;

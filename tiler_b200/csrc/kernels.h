@@ -40,6 +40,7 @@ int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t caus
 int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
                                 uint64_t extent, float eps, int8_t* codes, float* scales, tiler_cuda_status* st,
                                 int sm_count, cudaStream_t stream);
+void launch_bounded_wait_selftest(tiler_cuda_status* st, uint64_t limit_ns, cudaStream_t stream);
 void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
                              tiler_cuda_status* st, int sm_count, cudaStream_t stream);
 void launch_dequantize_i8_rows(const int8_t* codes, const float* scales, uint64_t rows, uint64_t extent, float* y,

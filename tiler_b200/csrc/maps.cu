@@ -17,6 +17,24 @@ __global__ void status_reset_kernel(tiler_cuda_status* st) {
 
 void launch_status_reset(tiler_cuda_status* st, cudaStream_t stream) { status_reset_kernel<<<1, 1, 0, stream>>>(st); }
 
+// The bounded wait every kernel uses, made to run out: an mbarrier phase that
+// nothing completes (one expected arrival, none made), waited on with a short
+// limit.  The wait gives up, counts a timeout in the status word and the
+// kernel returns; nothing is in flight, so the context stays usable.
+__global__ void bounded_wait_selftest_kernel(tiler_cuda_status* st, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait(&bar, 0, st, limit_ns);
+}
+
+void launch_bounded_wait_selftest(tiler_cuda_status* st, uint64_t limit_ns, cudaStream_t stream) {
+  bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(st, limit_ns);
+}
+
 // SiluF32Reference — silu.rs:78-110 (map) and :158-180 (scalar).
 __global__ void silu_kernel(const float* __restrict__ x, uint64_t n, float* __restrict__ y, tiler_cuda_status* st) {
   __shared__ double table[256];
