@@ -368,8 +368,10 @@ __device__ __forceinline__ uint32_t silu_bf16_fast(float x, bool* certain) {
   const float ax = fabsf(x);
   const float y = __fdividef(x, __fadd_rn(1.0f, __expf(-x)));
   const uint32_t b = __float_as_uint(y);
-  const float dist = fabsf(__fsub_rn((float)(int)(b & 0xffffu), 32768.0f));
-  *certain = ax < 80.0f && ((b >> 23) & 0xffu) != 0 && dist > __fadd_rn(__fmul_rn(2.0f, ax), 24.0f);
+  // the low 16 bits as a float without an int->float conversion: 2^23 + v - 2^23
+  const float low = __fsub_rn(__uint_as_float(0x4b000000u | (b & 0xffffu)), 8388608.0f);
+  const float dist = fabsf(__fsub_rn(low, 32768.0f));
+  *certain = ax < 80.0f && (b & 0x7f800000u) != 0 && dist > __fadd_rn(__fmul_rn(2.0f, ax), 24.0f);
   return (b + 0x7fffu + ((b >> 16) & 1u)) >> 16;
 }
 __device__ __noinline__ uint32_t silu_bf16_certified(float x, const double* table_hi, tiler_cuda_status* st) {
