@@ -136,14 +136,48 @@ def max_over_ranks(v, world):
     return float(t.item())
 
 
-def time_device(fn, steps, warmup, world, clocks=None):
+def cur_stream():
+    import torch
+    return torch.cuda.current_stream().cuda_stream
+
+
+GRAPH_CHUNK = 192  # launches per captured graph (a multiple of the rotating-buffer counts 2, 3, 4, 6, 8)
+
+
+def time_device(fn, steps, warmup, world, clocks=None, graph=False):
     """Runs warmup untimed steps, then times exactly `steps` calls of fn(i)
     with CUDA events on the current stream, barrier + synchronize on both
-    sides; returns (ms total, max over ranks)."""
+    sides; returns (ms total, max over ranks).  graph=True issues the timed
+    steps from CUDA graphs of GRAPH_CHUNK captured launches (and one graph for
+    the remainder), replayed back to back: the same kernels on the same
+    buffers, without the per-launch host overhead.  fn must launch on the
+    current stream only and must not synchronize."""
     import torch
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
+    replays = []
+    if graph:
+        try:
+            chunk = min(steps, GRAPH_CHUNK)
+            full, rest = divmod(steps, chunk)
+            cap = torch.cuda.Stream()
+            g_full = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_full, stream=cap):
+                for i in range(chunk):
+                    fn(i)
+            replays = [g_full] * full
+            if rest:
+                g_rest = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g_rest, stream=cap):
+                    for i in range(rest):
+                        fn(full * chunk + i)
+                replays.append(g_rest)
+            for g in set(replays):  # one untimed replay of each (uploads the graphs)
+                g.replay()
+        except Exception:  # noqa: BLE001 - capture refused: time plain launches
+            replays = []
+        torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
@@ -151,8 +185,12 @@ def time_device(fn, steps, warmup, world, clocks=None):
     ctx = clocks if clocks is not None else _Null()
     with ctx:
         e0.record(s)
-        for i in range(steps):
-            fn(i)
+        if replays:
+            for g in replays:
+                g.replay()
+        else:
+            for i in range(steps):
+                fn(i)
         e1.record(s)
         torch.cuda.synchronize()
     barrier(world)
@@ -250,9 +288,9 @@ def family_suite(fam, torch, world, steps_small, warmup):
     stream = torch.cuda.current_stream().cuda_stream
 
     def run_sum(i):
-        L.tiler_cuda_sum_f32(ctx, stream, xs[i % 4].data_ptr(), 1, n, C.byref(gs), ws.data_ptr(), ws.numel(),
+        L.tiler_cuda_sum_f32(ctx, cur_stream(), xs[i % 4].data_ptr(), 1, n, C.byref(gs), ws.data_ptr(), ws.numel(),
                              o.data_ptr())
-    ms = time_device(run_sum, steps_small * 4, warmup, world)
+    ms = time_device(run_sum, steps_small * 4, warmup, world, graph=True)
     rec("sum_f32_2^24", "GB/s", n * 4, ms, steps_small * 4, hbm)
     out["sum_f32_2^24"]["grouping"] = g
     del xs
@@ -261,19 +299,22 @@ def family_suite(fam, torch, world, steps_small, warmup):
     xb = [torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=gen).to(torch.bfloat16) for _ in range(6)]
     wb = (torch.rand(RMS_EXTENT, device=dev, generator=gen) + 0.5).to(torch.bfloat16)
     yb = [torch.empty_like(xb[0]) for _ in range(2)]
-    ms = time_device(lambda i: fam.rms_norm(xb[i % 6], wb, out=yb[i % 2], check=False), steps_small * 4, warmup, world)
+    ms = time_device(lambda i: fam.rms_norm(xb[i % 6], wb, out=yb[i % 2], check=False), steps_small * 4, warmup, world,
+                     graph=True)
     rec("rms_norm_bf16_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 4 + RMS_EXTENT * 2, ms, steps_small * 4, hbm)
     del xb, yb
 
     # softmax f32 [65536, 2048] with the causal block mask
     xsm = torch.randn(65536, 2048, device=dev, generator=gen) * 3
     ysm = torch.empty_like(xsm)
-    ms = time_device(lambda i: fam.softmax(xsm, causal_period=2048, out=ysm, check=False), steps_small, warmup, world)
+    ms = time_device(lambda i: fam.softmax(xsm, causal_period=2048, out=ysm, check=False), steps_small, warmup, world,
+                     graph=True)
     rec("softmax_f32_65536x2048_causal", "GB/s", 65536 * 2048 * 8, ms, steps_small, hbm)
     # the same causal mask as a program tensor [2048, 2048] (0 / -inf), added in the kernel
     col = torch.arange(2048, device=dev)
     mask = torch.where(col[None, :] > col[:, None], float("-inf"), 0.0).contiguous()
-    ms = time_device(lambda i: fam.softmax_masked(xsm, mask, out=ysm, check=False), steps_small, warmup, world)
+    ms = time_device(lambda i: fam.softmax_masked(xsm, mask, out=ysm, check=False), steps_small, warmup, world,
+                     graph=True)
     rec("softmax_masked_f32_65536x2048_mask_tensor", "GB/s", 65536 * 2048 * 8 + 2048 * 2048 * 4, ms, steps_small, hbm)
     del mask
     del xsm, ysm
@@ -281,7 +322,7 @@ def family_suite(fam, torch, world, steps_small, warmup):
     # quantize / decode f32 [16384, 4096]
     xq = [torch.randn(16384, 4096, device=dev, generator=gen) for _ in range(2)]
     codes, scales = fam.quantize_i8_rows(xq[0])
-    ms = time_device(lambda i: fam.quantize_i8_rows(xq[i % 2], check=False), steps_small, warmup, world)
+    ms = time_device(lambda i: fam.quantize_i8_rows(xq[i % 2], check=False), steps_small, warmup, world, graph=True)
     qbytes = 16384 * 4096 * 5 + 16384 * 4
     rec("quantize_i8_16384x4096", "GB/s", qbytes, ms, steps_small, hbm)
     yq = torch.empty(16384, 4096, device=dev)
@@ -290,15 +331,15 @@ def family_suite(fam, torch, world, steps_small, warmup):
     # fused RMS norm -> int8 quantize over the RMS config (x read once, y never written)
     xr = torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=gen)
     wr_ = torch.rand(RMS_EXTENT, device=dev, generator=gen) + 0.5
-    ms = time_device(lambda i: fam.rms_norm_quantize_i8(xr, wr_, check=False), steps_small, warmup, world)
+    ms = time_device(lambda i: fam.rms_norm_quantize_i8(xr, wr_, check=False), steps_small, warmup, world, graph=True)
     rec("rms_norm_quantize_i8_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 5 + RMS_EXTENT * 4 + RMS_ROWS * 4, ms,
         steps_small, hbm)
     del xr
 
     def run_dec(i):
-        L.tiler_cuda_dequantize_i8_rows(ctx, stream, None, codes.data_ptr(), scales.data_ptr(), 16384, 4096,
+        L.tiler_cuda_dequantize_i8_rows(ctx, cur_stream(), None, codes.data_ptr(), scales.data_ptr(), 16384, 4096,
                                         yq.data_ptr())
-    ms = time_device(run_dec, steps_small, warmup, world)
+    ms = time_device(run_dec, steps_small, warmup, world, graph=True)
     rec("dequantize_i8_16384x4096", "GB/s", qbytes, ms, steps_small, hbm)
     del xq, yq, codes, cd
 
@@ -307,14 +348,14 @@ def family_suite(fam, torch, world, steps_small, warmup):
     idss = [torch.randint(0, 128256, (8192,), device=dev, dtype=torch.int32, generator=gen) for _ in range(8)]
     ga = torch.empty(8192, 4096, device=dev, dtype=torch.bfloat16)
     ms = time_device(lambda i: fam.gather_rows(table, idss[i % 8], out=ga, check=False), steps_small * 4, warmup,
-                     world)
+                     world, graph=True)
     rec("gather_bf16_8192_of_128256x4096", "GB/s", 8192 * 4 + 8192 * 4096 * 4, ms, steps_small * 4, hbm)
 
     # bf16 contraction [8192,4096] x [4096,14336] + SiLU (W stored [N,K])
     wt = (torch.randn(14336, 4096, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
     cc = torch.empty(8192, 14336, device=dev, dtype=torch.bfloat16)
     gsteps = max(2, steps_small // 2)
-    ms = time_device(lambda i: fam.gemm_bf16(ga, wt, "silu", out=cc, check=False), gsteps, warmup, world)
+    ms = time_device(lambda i: fam.gemm_bf16(ga, wt, "silu", out=cc, check=False), gsteps, warmup, world, graph=True)
     rec("gemm_bf16_silu_8192x4096x14336", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps, tflops)
     if world > 1:
         # N-sharded contraction: each rank computes [8192, 14336/W] on its
@@ -326,7 +367,8 @@ def family_suite(fam, torch, world, steps_small, warmup):
         if (c1 - c0) % 256 == 0:
             ws_ = wt[c0:c1].contiguous()
             cl = torch.empty(8192, c1 - c0, device=dev, dtype=torch.bfloat16)
-            ms = time_device(lambda i: fam.gemm_bf16(ga, ws_, "silu", out=cl, check=False), gsteps, warmup, world)
+            ms = time_device(lambda i: fam.gemm_bf16(ga, ws_, "silu", out=cl, check=False), gsteps, warmup, world,
+                             graph=True)
             rec("gemm_bf16_silu_nsharded_local", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps, tflops * world)
             ms = time_device(lambda i: sharding.gemm_n_sharded(
                 ga, ws_, lambda a_, w_: fam.gemm_bf16(a_, w_, "silu", out=cl, check=False), assemble=False),
@@ -372,11 +414,11 @@ def run_tiler(args):
     stream = torch.cuda.current_stream().cuda_stream
 
     def step(i):
-        L.tiler_cuda_rms_norm_f32(ctx, stream, None, xs[i % nbuf].data_ptr(), w.data_ptr(), 0, RMS_ROWS,
+        L.tiler_cuda_rms_norm_f32(ctx, cur_stream(), None, xs[i % nbuf].data_ptr(), w.data_ptr(), 0, RMS_ROWS,
                                   RMS_EXTENT, EPS_BITS, ys[i % nbuf].data_ptr())
 
     clocks = ClockSampler(local) if rank == 0 else None
-    ms = time_device(step, args.steps, args.warmup, world, clocks=clocks)
+    ms = time_device(step, args.steps, args.warmup, world, clocks=clocks, graph=True)
     ms_step = ms / args.steps
     value = RMS_BYTES * world * args.steps / (ms / 1e3) / 1e9
     per_gpu = RMS_BYTES / (ms_step / 1e3) / 1e9
@@ -414,7 +456,9 @@ def run_tiler(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) x, U[0.5,1.5] w)",
             "config": {"workload": "rms_norm_f32 [8192,4096] eps=1e-6 (BASELINE configs[1])",
                        "l2": f"{nbuf} rotating input/output batches ({nbuf * 256} MB) > 126 MB L2",
-                       "parallelism": f"dp{world} (one [8192,4096] batch per GPU per step)"},
+                       "parallelism": f"dp{world} (one [8192,4096] batch per GPU per step)",
+                       "timing": f"CUDA events around CUDA graphs of {GRAPH_CHUNK} captured launches replayed back to "
+                                 "back (one launch per step); e2e from plain launches"},
             "gpu_launches": args.steps,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": RMS_ROWS * RMS_EXTENT * 4, "d2h_bytes_per_step": RMS_ROWS * RMS_EXTENT * 4,
