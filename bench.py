@@ -163,13 +163,13 @@ def time_device(fn, steps, warmup, world, clocks=None, graph=False):
             full, rest = divmod(steps, chunk)
             cap = torch.cuda.Stream()
             g_full = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g_full, stream=cap):
+            with torch.cuda.graph(g_full, stream=cap, capture_error_mode="thread_local"):
                 for i in range(chunk):
                     fn(i)
             replays = [g_full] * full
             if rest:
                 g_rest = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g_rest, stream=cap):
+                with torch.cuda.graph(g_rest, stream=cap, capture_error_mode="thread_local"):
                     for i in range(rest):
                         fn(full * chunk + i)
                 replays.append(g_rest)
