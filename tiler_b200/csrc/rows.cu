@@ -622,6 +622,9 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
   uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + 2048);  // one per row buffer
   float* rcp = reinterpret_cast<float*>(smem_raw + 2048 + 128);
   uint32_t* poisoned = reinterpret_cast<uint32_t*>(smem_raw + 2048 + 192);
+  // fold_end[w]: the denominator fold of row w stops here; past it every e is
+  // +0 exactly, and adding +0 to the positive running sum is the identity
+  uint32_t* fold_end = reinterpret_cast<uint32_t*>(smem_raw + 2048 + 224);
   float* bufs = reinterpret_cast<float*>(smem_raw + 2048 + 256);
   // warp 0 folds the denominators (the oldest warp, so the scheduler tends to
   // favour its dependent chain); warp w + 1 handles row w of each group.
@@ -711,40 +714,69 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
         const float sh = __fsub_rn(xv, m);
         return sh > -104.0f ? exp_cr_fast(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
       };
-      constexpr int EV = TILER_SMX_EXP_VECS;  // float4s per lane per step: 4 * EV independent exps
-      for (uint32_t v0 = lane; v0 < live4; v0 += 32 * EV) {
-        float xs[4 * EV];
-        uint32_t e[4 * EV], flagged = 0;
+      uint32_t last_nz = 0;  // one past this lane's last nonzero e (mask tensor only)
+      // TRACK (a mask tensor): arguments at or below -104 give +0 without
+      // certification and the last nonzero e is tracked, so the fold can stop
+      // there; the in-kernel causal mask already stops at the diagonal
+      auto exp_pass = [&](auto track) {
+        constexpr bool TRACK = decltype(track)::value;
+        constexpr int EV = TILER_SMX_EXP_VECS;  // float4s per lane per step: 4 * EV independent exps
+        for (uint32_t v0 = lane; v0 < live4; v0 += 32 * EV) {
+          float xs[4 * EV];
+          uint32_t e[4 * EV], flagged = 0;
 #pragma unroll
-        for (int h = 0; h < EV; ++h) {
-          const uint32_t v = v0 + 32 * h;
-          const float4 q = v < live4 ? b4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
-          xs[4 * h] = q.x; xs[4 * h + 1] = q.y; xs[4 * h + 2] = q.z; xs[4 * h + 3] = q.w;
-        }
+          for (int h = 0; h < EV; ++h) {
+            const uint32_t v = v0 + 32 * h;
+            const float4 q = v < live4 ? b4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+            xs[4 * h] = q.x; xs[4 * h + 1] = q.y; xs[4 * h + 2] = q.z; xs[4 * h + 3] = q.w;
+          }
 #pragma unroll
-        for (int i = 0; i < 4 * EV; ++i) {
-          const float sh = __fsub_rn(xs[i], m);
-          bool ok;
-          e[i] = exp_cr_bits(sh, table, &ok);
-          flagged |= ((ok && sh > -104.0f) ? 0u : 1u) << i;
-        }
-        if (__any_sync(__activemask(), flagged != 0)) {  // rare: certify or special-case the flagged ones
+          for (int i = 0; i < 4 * EV; ++i) {
+            const float sh = __fsub_rn(xs[i], m);
+            bool ok;
+            e[i] = exp_cr_bits(sh, table, &ok);
+            if (TRACK) {
+              // e^sh = +0 for sh <= -104 (silu.rs:224-235 guards): no certification needed
+              const bool zero = !(sh > -104.0f) && !is_nan_bits(sh);
+              if (zero) e[i] = 0u;
+              flagged |= ((ok && sh > -104.0f) || zero ? 0u : 1u) << i;
+            } else {
+              flagged |= ((ok && sh > -104.0f) ? 0u : 1u) << i;
+            }
+          }
+          if (__any_sync(__activemask(), flagged != 0)) {  // rare: certify or special-case the flagged ones
 #pragma unroll
-          for (int i = 0; i < 4 * EV; ++i)
-            if ((flagged >> i) & 1u) e[i] = __float_as_uint(softmax_exp_slow(__fsub_rn(xs[i], m), table, st));
-        }
+            for (int i = 0; i < 4 * EV; ++i)
+              if ((flagged >> i) & 1u) e[i] = __float_as_uint(softmax_exp_slow(__fsub_rn(xs[i], m), table, st));
+          }
 #pragma unroll
-        for (int h = 0; h < EV; ++h) {
-          const uint32_t v = v0 + 32 * h;
-          if (v < live4)
-            b4[v] = make_float4(__uint_as_float(e[4 * h]), __uint_as_float(e[4 * h + 1]), __uint_as_float(e[4 * h + 2]),
-                                __uint_as_float(e[4 * h + 3]));
+          for (int h = 0; h < EV; ++h) {
+            const uint32_t v = v0 + 32 * h;
+            if (v < live4) {
+              b4[v] = make_float4(__uint_as_float(e[4 * h]), __uint_as_float(e[4 * h + 1]),
+                                  __uint_as_float(e[4 * h + 2]), __uint_as_float(e[4 * h + 3]));
+              if (TRACK) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  if (e[4 * h + i] != 0u) last_nz = max(last_nz, v * 4 + i + 1);
+              }
+            }
+          }
         }
+      };
+      if (mask) exp_pass(std::true_type{});
+      else exp_pass(std::false_type{});
+      for (uint32_t c = live4 * 4 + lane; c < live; c += 32) {
+        b[c] = exp_of(b[c]);
+        if (mask && __float_as_uint(b[c]) != 0u) last_nz = max(last_nz, c + 1);
       }
-      for (uint32_t c = live4 * 4 + lane; c < live; c += 32) b[c] = exp_of(b[c]);
       for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) b[c] = 0.0f;
       for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (lane == 0) poisoned[warp] = bad;
+      if (mask) last_nz = __reduce_max_sync(0xffffffffu, last_nz);
+      if (lane == 0) {
+        poisoned[warp] = bad;
+        fold_end[warp] = mask ? max(last_nz, 1u) : live;  // at least e_0, the seed
+      }
     }
     if (!__syncthreads_and(ok)) {
       if (lane == 0 && !chain_warp) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -757,8 +789,7 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
     if (chain_warp) {
       // ---- chain warp: lane r folds row r's denominator ------------------------
       if (lane < n) {
-        const uint64_t row = row0 + lane;
-        const uint32_t live = causal ? (uint32_t)umin64((row_offset + row) % period + 1, extent) : ext;
+        const uint32_t live = fold_end[lane];  // the unmasked columns up to the last nonzero e
         const uint32_t base = smem_u32(bufs + (uint64_t)lane * ext);
         const float* b = bufs + (uint64_t)lane * ext;
         float acc = b[0];
