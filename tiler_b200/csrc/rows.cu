@@ -730,6 +730,24 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
             const float4 q = v < live4 ? b4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
             xs[4 * h] = q.x; xs[4 * h + 1] = q.y; xs[4 * h + 2] = q.z; xs[4 * h + 3] = q.w;
           }
+          if (TRACK) {
+            // a step whose arguments are all at or below -104 (a masked stretch)
+            // is +0 throughout: skip the evaluation when the whole warp agrees
+            bool low = true;
+#pragma unroll
+            for (int i = 0; i < 4 * EV; ++i) {
+              const float sh = __fsub_rn(xs[i], m);
+              low = low && !(sh > -104.0f) && !is_nan_bits(sh);
+            }
+            if (__all_sync(__activemask(), low)) {
+#pragma unroll
+              for (int h = 0; h < EV; ++h) {
+                const uint32_t v = v0 + 32 * h;
+                if (v < live4) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+              }
+              continue;
+            }
+          }
 #pragma unroll
           for (int i = 0; i < 4 * EV; ++i) {
             const float sh = __fsub_rn(xs[i], m);
