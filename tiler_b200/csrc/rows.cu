@@ -582,6 +582,7 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
 //      recorded as a poisoned row;
 //   3. the chain warp folds all G denominators at once, lane w folding row
 //      w strictly, d = (((e_0 + e_1) + e_2) + ...), up to the diagonal only
+//      with the causal mask, up to the last nonzero e with a mask tensor
 //      (adding +0.0 to a positive running sum is the identity), r = 1/d;
 //   4. warp w forms out_i = e_i * r in place over the live columns and
 //      writes the row back with one bulk store.
