@@ -1,0 +1,46 @@
+"""The target profile and payload provenance rows, checked against the
+library and the build (no GPU)."""
+import re
+
+from tiler_b200 import _native as N
+from tiler_b200 import provider, target_profile as tp
+
+
+def test_profile_rows_match_what_the_backend_checks():
+    prof = tp.target_profile()
+    caps = dict(prof["capability"])
+    assert caps["max_threads_per_workgroup"] == 1024
+    assert caps["local_memory_bytes"] == 232448  # 227 KB opt-in shared memory per block
+    assert caps["index_arithmetic"] == "CompleteU64" and caps["device_address_width"] == "Bits64"
+    # the subgroup width the payload validation requires (an equality)
+    (sub, support), = prof["subgroup_realization"]
+    assert sub["width"] == provider.SUBGROUP_WIDTH == 32 and support == "Supported"
+    numerics = {(axis, behaviour): support for _, axis, behaviour, support in prof["numerics"]}
+    assert numerics[("input_subnormals", "Preserve")] == "Exact"
+    assert numerics[("result_subnormals", "FlushToZero{PreservesSign}")] == "Unsupported"
+    assert numerics[("contraction", "Forbidden")] == "Exact"
+    assert numerics[("contraction", "Permitted")] == "Unsupported"
+    assert numerics[("approximate_intrinsics", "Forbidden")] == "Exact"
+    # device facts override the stated limits
+    caps = dict(tp.capability_rows({"max_threads_per_block": 512, "smem_per_block_optin": 100}))
+    assert caps["max_threads_per_workgroup"] == 512 and caps["local_memory_bytes"] == 100
+
+
+def test_payload_provenance_states_the_build():
+    prov = tp.payload_provenance()
+    assert prov["target"] == "sm_100a" and prov["platform"] == "Unversioned"
+    flags = prov["compile_flags"]
+    # the numerics the profile declares rest on these flags
+    assert "-fmad=false" in flags and not any("ftz" in f or "fast-math" in f for f in flags)
+    assert "arch=compute_100a,code=sm_100a" in flags
+    assert re.match(r"nvcc", prov["toolchain"])
+
+
+def test_payload_entries_are_the_registry():
+    L = N.lib()
+    entries = tp.payload_entries()
+    assert len(entries) == L.tiler_cuda_entry_count() > 10
+    for e in entries:
+        assert e["symbol"] == "tiler_cuda." + e["entry_key"]
+    keys = {e["entry_key"] for e in entries}
+    assert {"rms_norm_f32", "softmax_f32", "gemm_bf16", "sum_f32.grouped", "rms_norm_quantize_i8"} <= keys

@@ -10,7 +10,8 @@ LIB = os.path.join(HERE, "libtiler_cuda.so")
 
 
 def build(verbose: bool = False) -> str:
-    os.makedirs(os.path.join(HERE, "..", "_work"), exist_ok=True)
+    """make -C csrc; the ptxas report (registers, spills, shared memory per
+    kernel) goes to tiler_b200/_build/ptxas.log."""
     r = subprocess.run(["make", "-C", CSRC], capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
