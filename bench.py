@@ -304,6 +304,16 @@ def family_suite(fam, torch, world, steps_small, warmup):
     rec("rms_norm_bf16_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 4 + RMS_EXTENT * 2, ms, steps_small * 4, hbm)
     del xb, yb
 
+    # elementwise maps f32 [8192, 4096]: certified SiLU, and (x*a)+b with rank-0 a, b
+    xm = [torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=gen) * 4 for _ in range(3)]
+    ym = [torch.empty_like(xm[0]) for _ in range(2)]
+    ms = time_device(lambda i: fam.silu(xm[i % 3], out=ym[i % 2], check=False), steps_small * 2, warmup, world, graph=True)
+    rec("silu_f32_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 8, ms, steps_small * 2, hbm)
+    sa, sb = torch.tensor(1.5, device=dev), torch.tensor(-0.25, device=dev)
+    ms = time_device(lambda i: fam.scale_bias(xm[i % 3], sa, sb, out=ym[i % 2]), steps_small * 2, warmup, world, graph=True)
+    rec("scale_bias_f32_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 8, ms, steps_small * 2, hbm)
+    del xm, ym
+
     # softmax f32 [65536, 2048] with the causal block mask
     xsm = torch.randn(65536, 2048, device=dev, generator=gen) * 3
     ysm = torch.empty_like(xsm)

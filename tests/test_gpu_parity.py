@@ -322,6 +322,15 @@ def test_silu_random_bit_patterns_match_oracle(fam, oracle_lib):
         assert_bits_equal(got, want, "silu")
 
 
+def test_silu_dense_sweep_and_ragged_tail_match_oracle(fam, oracle_lib):
+    """x dense over [-120, 120] (every exponent band of exp(-x), both range
+    guards at -89 and 104) at a length that leaves a 3-element tail."""
+    x = np.linspace(-120, 120, (1 << 21) + 3, dtype=np.float32)
+    got = host(fam.silu(cuda(x)))
+    _, want = oracle_lib.silu_f32(x)
+    assert_bits_equal(got, want, "silu sweep")
+
+
 def test_softmax_exp_band_sweep_matches_oracle(fam, oracle_lib):
     """Every exponent band the certified exp covers: rows of x with max 0, so
     exp(x) is evaluated on [-104, 0] densely."""
@@ -330,6 +339,23 @@ def test_softmax_exp_band_sweep_matches_oracle(fam, oracle_lib):
     got = host(fam.softmax(cuda(x)))
     _, want = oracle_lib.softmax_f32(x, nthreads=8)
     assert_bits_equal(got, want, "exp sweep")
+
+
+@pytest.mark.parametrize("n,offset", [(1, 0), (3, 0), (4, 0), (2047, 0), (2048 * 5 + 1, 0), (9999, 1), (9999, 3),
+                                      (3_000_001, 0)])
+def test_elementwise_maps_sizes_and_alignment(fam, oracle_lib, n, offset):
+    """The staged maps (16-byte aligned x and y: bulk-copied tiles, a partial
+    last tile, a tail of n % 4 elements) and the unaligned grid-stride form."""
+    x = seeded_normal(5, n + offset, std=30.0)
+    xd = cuda(x)[offset:]
+    yd = torch.empty(n + offset, device="cuda")[offset:]
+    got = host(fam.silu(xd, out=yd))
+    _, want = oracle_lib.silu_f32(x[offset:])
+    assert_bits_equal(got, want, f"silu n={n} offset={offset}")
+    a, b = np.float32(0.75), np.float32(1.0e-3)
+    got = host(fam.scale_bias(xd, torch.tensor(a).cuda(), torch.tensor(b).cuda(), out=yd))
+    _, want = oracle_lib.scale_bias_f32(x[offset:], a, b)
+    assert_bits_equal(got, want, f"scale_bias n={n} offset={offset}")
 
 
 def test_scale_bias_matches_oracle(fam, oracle_lib):

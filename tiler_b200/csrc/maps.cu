@@ -35,35 +35,38 @@ void launch_bounded_wait_selftest(tiler_cuda_status* st, uint64_t limit_ns, cuda
   bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(st, limit_ns);
 }
 
-// SiluF32Reference — silu.rs:78-110 (map) and :158-180 (scalar).
-__global__ void silu_kernel(const float* __restrict__ x, uint64_t n, float* __restrict__ y, tiler_cuda_status* st) {
-  __shared__ double table[256];
-  load_exp_table(table);
-  __syncthreads();
-  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  const uint64_t tid = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (((uintptr_t)x % 16 == 0) && ((uintptr_t)y % 16 == 0)) {
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    float4* y4 = reinterpret_cast<float4*>(y);
-    for (uint64_t v = tid; v < n / 4; v += stride) {
-      float4 q = __ldcs(x4 + v);
-      q.x = silu_cr_fast(q.x, table, st);
-      q.y = silu_cr_fast(q.y, table, st);
-      q.z = silu_cr_fast(q.z, table, st);
-      q.w = silu_cr_fast(q.w, table, st);
-      st_global_stream(y4 + v, q);
-    }
-    for (uint64_t i = n / 4 * 4 + tid; i < n; i += stride) y[i] = silu_cr(x[i], table, st);
-  } else {
-    for (uint64_t i = tid; i < n; i += stride) y[i] = silu_cr(x[i], table, st);
-  }
+// silu_cr out of line, so the rare flagged arguments cost the common path no
+// registers
+__device__ __noinline__ float silu_cr_outlined(float x, const double* table, tiler_cuda_status* st) {
+  return silu_cr(x, table, st);
 }
 
-void launch_silu(const float* x, uint64_t n, float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
-  if (n == 0) return;
-  const uint64_t want = (n / 4 + 255) / 256 + 1;
-  silu_kernel<<<(unsigned)std::min<uint64_t>(want, (uint64_t)sm_count * 8), 256, 0, stream>>>(x, n, y, st);
-}
+// SiLU of four values: silu_cr_fast's path for x in (-89, 104) with the
+// certified exp branch-free; the flagged values (out of range, NaN, or an exp
+// near a rounding midpoint) take silu_cr in one warp-uniform branch.
+struct SiluOp {
+  const double* table;
+  tiler_cuda_status* st;
+  __device__ __forceinline__ float4 operator()(float4 q) const {
+    const float xs[4] = {q.x, q.y, q.z, q.w};
+    float r[4];
+    uint32_t flagged = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      bool ok;
+      const float e = __uint_as_float(exp_cr_bits(-xs[i], table, &ok));
+      r[i] = __fdiv_rn(xs[i], __fadd_rn(1.0f, e));
+      flagged |= ((ok && xs[i] > -89.0f && xs[i] < 104.0f) ? 0u : 1u) << i;
+    }
+    if (__any_sync(__activemask(), flagged != 0)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if ((flagged >> i) & 1u) r[i] = silu_cr_outlined(xs[i], table, st);
+    }
+    return make_float4(r[0], r[1], r[2], r[3]);
+  }
+  __device__ __forceinline__ float operator()(float x) const { return silu_cr(x, table, st); }
+};
 
 // multiply-f32 then add-f32, two roundings (standard.rs:105-120,
 // evaluate.rs:448-485), NaN canonicalized after each operation.
@@ -71,6 +74,141 @@ __device__ __forceinline__ float scale_bias1(float x, float a, float b) {
   return canon(__fadd_rn(canon(__fmul_rn(x, a)), b));
 }
 
+struct ScaleBiasOp {
+  float a, b;
+  __device__ __forceinline__ float4 operator()(float4 q) const {
+    return make_float4(scale_bias1(q.x, a, b), scale_bias1(q.y, a, b), scale_bias1(q.z, a, b),
+                       scale_bias1(q.w, a, b));
+  }
+  __device__ __forceinline__ float operator()(float x) const { return scale_bias1(x, a, b); }
+};
+
+// Staged elementwise map over a flat f32 array whose input and output are
+// 16-byte aligned.  A persistent CTA walks tiles of kMapTile floats with a
+// ring of kMapStages shared-memory buffers: one bulk load per tile (issued
+// kMapStages - 1 tiles ahead), the map applied in place, one bulk store per
+// tile.  The reads in flight are the copy engine's, so they do not depend on
+// the map's register footprint.  The last n % 4 elements are done by block 0
+// with plain accesses.
+constexpr int kMapThreads = 256;
+constexpr uint32_t kMapTile = 2048;  // floats (8 KB)
+constexpr uint32_t kMapStages = 4;
+constexpr int kMapCtasPerSm = 6;
+constexpr size_t kMapSmem = (size_t)kMapStages * kMapTile * 4 + kMapStages * 8;
+
+template <class Op>
+__device__ __forceinline__ void staged_map(const float* __restrict__ x, uint64_t n, float* __restrict__ y, Op op,
+                                           float* buf, uint64_t* full, tiler_cuda_status* st) {
+  __shared__ int abort_flag;
+  const uint64_t n4 = n / 4 * 4;
+  const uint64_t tiles = (n4 + kMapTile - 1) / kMapTile;
+  const uint64_t pol = policy_evict_first();
+  auto tile_floats = [&](uint64_t t) -> uint32_t {
+    return (uint32_t)umin64(kMapTile, n4 - t * kMapTile);
+  };
+  auto issue = [&](uint64_t t, uint32_t b) {
+    const uint32_t bytes = tile_floats(t) * 4;
+    mbar_arrive_expect_tx(&full[b], bytes);
+    bulk_g2s(buf + b * kMapTile, x + t * kMapTile, bytes, &full[b], pol);
+  };
+  if (threadIdx.x == 0) {
+    for (uint32_t b = 0; b < kMapStages; ++b) mbar_init(&full[b], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+    for (uint32_t b = 0; b + 1 < kMapStages; ++b)
+      if (blockIdx.x + (uint64_t)b * gridDim.x < tiles) issue(blockIdx.x + (uint64_t)b * gridDim.x, b);
+  }
+  __syncthreads();
+  uint32_t k = 0;
+  for (uint64_t t = blockIdx.x; t < tiles; t += gridDim.x, ++k) {
+    const uint32_t b = k % kMapStages;
+    if (!mbar_wait(&full[b], (k / kMapStages) & 1, st)) abort_flag = 1;
+    __syncthreads();
+    if (abort_flag) break;
+    const uint32_t nf = tile_floats(t);
+    float4* v = reinterpret_cast<float4*>(buf + b * kMapTile);
+    for (uint32_t i = threadIdx.x; i < nf / 4; i += kMapThreads) v[i] = op(v[i]);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(y + t * kMapTile),
+                   "r"(smem_u32(buf + b * kMapTile)), "r"(nf * 4)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      // refill the buffer stored one tile ago once that store has read it
+      // (this tile's store stays in flight)
+      const uint64_t nt = t + (uint64_t)(kMapStages - 1) * gridDim.x;
+      if (nt < tiles) {
+        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        issue(nt, (k + kMapStages - 1) % kMapStages);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    // loads still in flight (abort) must land before shared memory is released
+    if (abort_flag)
+      for (uint32_t j = 0; j + 1 < kMapStages; ++j) {
+        const uint32_t kk = k + j;
+        if (blockIdx.x + (uint64_t)kk * gridDim.x < tiles)
+          (void)mbar_wait(&full[kk % kMapStages], (kk / kMapStages) & 1, nullptr);
+      }
+  }
+  if (blockIdx.x == 0)
+    for (uint64_t i = n4 + threadIdx.x; i < n; i += kMapThreads) y[i] = op(x[i]);
+}
+
+// SiluF32Reference — silu.rs:78-110 (map) and :158-180 (scalar).
+__global__ void __launch_bounds__(kMapThreads, 5) silu_staged_kernel(const float* __restrict__ x, uint64_t n,
+                                                                  float* __restrict__ y, tiler_cuda_status* st) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ double table[256];
+  load_exp_table(table);
+  staged_map(x, n, y, SiluOp{table, st}, reinterpret_cast<float*>(smem_raw),
+             reinterpret_cast<uint64_t*>(smem_raw + (size_t)kMapStages * kMapTile * 4), st);
+}
+
+__global__ void scale_bias_staged_kernel(const float* __restrict__ x, uint64_t n, const float* __restrict__ a,
+                                         const float* __restrict__ b, float* __restrict__ y, tiler_cuda_status* st) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  staged_map(x, n, y, ScaleBiasOp{__ldg(a), __ldg(b)}, reinterpret_cast<float*>(smem_raw),
+             reinterpret_cast<uint64_t*>(smem_raw + (size_t)kMapStages * kMapTile * 4), st);
+}
+
+template <class K>
+static unsigned staged_map_grid(K kernel, uint64_t n, int sm_count) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMapSmem);
+  cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  int resident = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kernel, kMapThreads, kMapSmem) != cudaSuccess ||
+      resident < 1)
+    resident = 1;
+  const uint64_t tiles = (n / 4 * 4 + kMapTile - 1) / kMapTile;
+  return (unsigned)std::max<uint64_t>(1, umin64(tiles, (uint64_t)sm_count * std::min(resident, kMapCtasPerSm)));
+}
+
+// The unaligned form: grid-stride over single elements.
+__global__ void silu_kernel(const float* __restrict__ x, uint64_t n, float* __restrict__ y, tiler_cuda_status* st) {
+  __shared__ double table[256];
+  load_exp_table(table);
+  __syncthreads();
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += stride) y[i] = silu_cr(x[i], table, st);
+}
+
+void launch_silu(const float* x, uint64_t n, float* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream) {
+  if (n == 0) return;
+  if ((uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0) {
+    silu_staged_kernel<<<staged_map_grid(silu_staged_kernel, n, sm_count), kMapThreads, kMapSmem, stream>>>(x, n, y,
+                                                                                                           st);
+    return;
+  }
+  const uint64_t want = (n + 255) / 256;
+  silu_kernel<<<(unsigned)std::min<uint64_t>(want, (uint64_t)sm_count * 8), 256, 0, stream>>>(x, n, y, st);
+}
+
+// The general form (tensor a / b, or unaligned): grid-stride, float4 where
+// the pointers allow.
 __global__ void scale_bias_kernel(const float* __restrict__ x, uint64_t n, const float* __restrict__ a, int a_scalar,
                                   const float* __restrict__ b, int b_scalar, float* __restrict__ y) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -82,7 +220,8 @@ __global__ void scale_bias_kernel(const float* __restrict__ x, uint64_t n, const
   if (vec) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     float4* y4 = reinterpret_cast<float4*>(y);
-    for (uint64_t v = tid; v < n / 4; v += stride) {
+    const uint64_t nv = n / 4;
+    for (uint64_t v = tid; v < nv; v += stride) {
       const float4 q = __ldcs(x4 + v);
       const float4 av = a_scalar ? make_float4(as, as, as, as) : __ldcs(reinterpret_cast<const float4*>(a) + v);
       const float4 bv = b_scalar ? make_float4(bs, bs, bs, bs) : __ldcs(reinterpret_cast<const float4*>(b) + v);
@@ -98,6 +237,13 @@ __global__ void scale_bias_kernel(const float* __restrict__ x, uint64_t n, const
 void launch_scale_bias(const float* x, uint64_t n, const float* a, int a_scalar, const float* b, int b_scalar,
                        float* y, int sm_count, cudaStream_t stream) {
   if (n == 0) return;
+  if (a_scalar && b_scalar && (uintptr_t)x % 16 == 0 && (uintptr_t)y % 16 == 0) {
+    // the broadcast form through the staged map (a wait that runs out ends the
+    // kernel early; this entry has no status word to report it in)
+    scale_bias_staged_kernel<<<staged_map_grid(scale_bias_staged_kernel, n, sm_count), kMapThreads, kMapSmem,
+                               stream>>>(x, n, a, b, y, nullptr);
+    return;
+  }
   const uint64_t want = (n / 4 + 255) / 256 + 1;
   scale_bias_kernel<<<(unsigned)std::min<uint64_t>(want, (uint64_t)sm_count * 8), 256, 0, stream>>>(
       x, n, a, a_scalar, b, b_scalar, y);

@@ -359,9 +359,9 @@ def dequantize_affine_u8(codes: torch.Tensor, scale: float, zero_point: int, max
 
 # ---- maps ---------------------------------------------------------------------
 
-def silu(x: torch.Tensor, check=True) -> torch.Tensor:
+def silu(x: torch.Tensor, out=None, check=True) -> torch.Tensor:
     """SiluF32Reference (silu.rs:78-180)."""
-    y = torch.empty_like(x)
+    y = torch.empty_like(x) if out is None else out
     st = _status() if check else None
     _check(N.lib().tiler_cuda_silu_f32(context(), _stream(), st.ptr if st else 0, _ptr(x), x.numel(), _ptr(y)),
            "silu")
@@ -370,13 +370,13 @@ def silu(x: torch.Tensor, check=True) -> torch.Tensor:
     return y
 
 
-def scale_bias(x: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+def scale_bias(x: torch.Tensor, a: torch.Tensor, b: torch.Tensor, out=None) -> torch.Tensor:
     """multiply-f32 then add-f32 (standard.rs:105-120): y = (x*a)+b, two
     roundings; a rank-0 ``a``/``b`` broadcasts, otherwise it has x's size."""
     for t in (a, b):
         if t.dim() != 0 and t.numel() != x.numel():
             raise ValueError("scale_bias operands are rank-0 or the size of x")
-    y = torch.empty_like(x)
+    y = torch.empty_like(x) if out is None else out
     _check(N.lib().tiler_cuda_scale_bias_f32(context(), _stream(), _ptr(x), x.numel(), _ptr(a), int(a.dim() == 0),
                                              _ptr(b), int(b.dim() == 0), _ptr(y)), "scale_bias")
     return y
