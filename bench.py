@@ -513,6 +513,12 @@ def run_profile_case(family: str, launches: int):
         x = torch.randn(65536, 2048, device=dev, generator=g) * 3
         y = torch.empty_like(x)
         run = lambda: fam.softmax(x, causal_period=2048, out=y, check=False)
+    elif family in ("silu", "scale_bias"):
+        x = torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=g) * 4
+        y = torch.empty_like(x)
+        sa, sb = torch.tensor(1.5, device=dev), torch.tensor(-0.25, device=dev)
+        run = (lambda: fam.silu(x, out=y, check=False)) if family == "silu" else \
+            (lambda: fam.scale_bias(x, sa, sb, out=y))
     elif family == "sum":
         x = torch.rand(1 << 24, device=dev, generator=g) * 2 - 1
         gr = fam.plan_grouping(1, 1 << 24)

@@ -192,6 +192,18 @@ def test_reference_vocabulary_sums_match_the_oracle(fam, oracle_lib):
                           oracle_lib.cooperative_sum(x, 32, 8, 16, pm)[1])
 
 
+def test_serial_folds_at_every_batch_boundary(fam, oracle_lib):
+    """The strict and partitioned folds at lengths around the load batch (8):
+    1..40 and a few long ragged rows."""
+    for count in list(range(1, 41)) + [1000, 4097]:
+        x = seeded_normal(count, 3 * count).reshape(3, count) * 1e3
+        assert_bits_equal(host(fam.strict_sum_f32(cuda(x))), oracle_lib.strict_sum(x)[1], f"strict {count}")
+    for parts, per in [(3, 7), (5, 9), (2, 17), (4, 24)]:
+        x = seeded_normal(per, 2 * parts * per).reshape(2, parts * per) * 1e3
+        assert_bits_equal(host(fam.partitioned_sum_f32(cuda(x), parts, per)),
+                          oracle_lib.partitioned_sum(x, parts, per)[1], f"partitioned {parts}x{per}")
+
+
 def test_empty_sum_is_positive_zero_and_empty_max_is_refused(fam):
     x = torch.empty((3, 0), dtype=torch.float32, device="cuda")
     assert bits_of(host(fam.strict_sum_f32(x))) == [0, 0, 0]
@@ -599,3 +611,15 @@ def test_route_a_program_through_the_runtime_adapter(fam, oracle_lib):
     g = fam.plan_grouping(1, x.size)
     assert_bits_equal(host(out[1]).reshape(1), oracle_lib.grid_fold(x.reshape(-1), g)[1])
     assert ad.trace.index("commit") < ad.trace.index("dispatch")
+
+
+def test_saturated_parallel_fold_steps_is_measured(fam):
+    """The measured cost row: the dispatch sweep over the three sum
+    strategies fits the work-span model with a positive P and step."""
+    from tiler_b200 import target_profile as tp
+    cells = tp.measure_fold_cells(fam, torch, repeats=5)
+    assert {c["strategy"] for c in cells} == {"strict", "partitioned", "grouped"}
+    fit = tp.fit_work_span(cells)
+    assert fit["parallel_steps"] > 32 and fit["step_s"] > 0 and fit["residual"] < 1.0
+    (key, value, _), = tp.cost_rows(round(fit["parallel_steps"]))
+    assert key == tp.COST_ROW_KEY and value > 0

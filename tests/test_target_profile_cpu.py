@@ -44,3 +44,25 @@ def test_payload_entries_are_the_registry():
         assert e["symbol"] == "tiler_cuda." + e["entry_key"]
     keys = {e["entry_key"] for e in entries}
     assert {"rms_norm_f32", "softmax_f32", "gemm_bf16", "sum_f32.grouped", "rms_norm_quantize_i8"} <= keys
+
+
+def test_work_span_fit_recovers_a_known_model():
+    """The cost-row fit on cells generated from a stated model (P = 4736
+    steps at once, 3 us per stage, 2 ns per step) with 2 % noise."""
+    import numpy as np
+    rng = np.random.default_rng(4)
+    P, enc, step = 4736.0, 3e-6, 2e-9
+    cells = []
+    for rows, count in [(128, 256), (1024, 256), (8192, 256), (65536, 64), (262144, 64), (32, 4096), (512, 2048),
+                        (4096, 1024), (16384, 512), (16, 16384)]:
+        for stages in ([(rows * count, count)], [(rows * count, count // 16), (rows * 16, 16)]):
+            t = sum(enc + max(w / P, d) * step for w, d in stages) * (1 + 0.02 * rng.standard_normal())
+            cells.append({"stages": stages, "seconds": t})
+    fit = tp.fit_work_span(cells)
+    assert abs(fit["parallel_steps"] / P - 1) < 0.1
+    assert abs(fit["step_s"] / step - 1) < 0.1
+    assert fit["residual"] < 0.05
+    prof = tp.target_profile(measured_fold_steps=round(fit["parallel_steps"]))
+    (key, value, scope), = prof["cost"]
+    assert key == "cost.saturated-parallel-fold-steps" and scope == "MeasuredEnvironment" and value > 0
+    assert tp.target_profile()["cost"] == []  # silence without a measurement

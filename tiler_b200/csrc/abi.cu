@@ -110,8 +110,8 @@ struct Entry {
 const Entry kEntries[] = {
     {"tiler_cuda.sum_f32.grouped", (const void*)grouped_fold_kernel<0, 4>, 512, 0},
     {"tiler_cuda.max_f32.grouped", (const void*)grouped_fold_kernel<1, 4>, 512, 0},
-    {"tiler_cuda.sum_f32.strict", (const void*)strict_sum_kernel, 128, 0},
-    {"tiler_cuda.sum_f32.partitioned", (const void*)partial_sums_kernel, 128, 0},
+    {"tiler_cuda.sum_f32.strict", (const void*)serial_folds_kernel<true>, kSerialFoldThreads, 0},
+    {"tiler_cuda.sum_f32.partitioned", (const void*)serial_folds_kernel<false>, kSerialFoldThreads, 0},
     {"tiler_cuda.sum_f32.cooperative", (const void*)cooperative_sum_kernel, 1024, 0},
     {"tiler_cuda.rms_norm_f32", (const void*)rms_norm_kernel<false>, kRmsThreads, kRmsSmemBytes},
     {"tiler_cuda.rms_norm_bf16", (const void*)rms_norm_kernel<true>, kRmsThreads, kRmsSmemBytes},

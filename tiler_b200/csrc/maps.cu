@@ -159,7 +159,7 @@ __device__ __forceinline__ void staged_map(const float* __restrict__ x, uint64_t
 }
 
 // SiluF32Reference — silu.rs:78-110 (map) and :158-180 (scalar).
-__global__ void __launch_bounds__(kMapThreads, 5) silu_staged_kernel(const float* __restrict__ x, uint64_t n,
+__global__ void __launch_bounds__(kMapThreads) silu_staged_kernel(const float* __restrict__ x, uint64_t n,
                                                                   float* __restrict__ y, tiler_cuda_status* st) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ double table[256];

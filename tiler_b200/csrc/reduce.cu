@@ -216,41 +216,104 @@ void launch_grouped_fold(int op, const float* x, uint64_t rows, uint64_t count, 
 
 // ---- reference-vocabulary groupings ------------------------------------------
 
-// strict_sum (evaluate.rs:498-589): one thread folds one row in order.
-__global__ void strict_sum_kernel(const float* __restrict__ x, uint64_t rows, uint64_t count,
-                                  float* __restrict__ out) {
-  uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (r >= rows) return;
-  if (count == 0) { out[r] = 0.0f; return; }
-  const float* s = x + r * count;
-  float acc = s[0];
-  for (uint64_t i = 1; i < count; ++i) acc = __fadd_rn(acc, s[i]);
-  out[r] = canon(acc);
+// A strict left fold of s[0..n) seeded at s[0] (n >= 1), by one warp: each
+// 32-element batch is loaded coalesced (lane j holds element j) and folded in
+// order by broadcasting lane j's value at step j, every lane carrying the
+// same accumulator.  kFoldAhead batches are loaded ahead of the one being
+// folded, so the chain of dependent adds, not the load latency, sets the
+// pace.  The result is returned in every lane.
+constexpr int kFoldAhead = 8;
+__device__ __forceinline__ float warp_serial_fold(const float* __restrict__ s, uint64_t n, uint32_t lane) {
+  const uint64_t nb = (n + 31) / 32;
+  float pf[kFoldAhead];
+#pragma unroll
+  for (int d = 0; d < kFoldAhead; ++d) {
+    const uint64_t idx = (uint64_t)d * 32 + lane;
+    pf[d] = idx < n ? __ldcg(s + idx) : 0.0f;
+  }
+  float acc = __shfl_sync(0xffffffffu, pf[0], 0);
+  for (uint64_t b0 = 0; b0 < nb; b0 += kFoldAhead) {
+#pragma unroll
+    for (int d = 0; d < kFoldAhead; ++d) {
+      const uint64_t b = b0 + d;
+      const float v = pf[d];
+      const uint64_t nidx = (b + kFoldAhead) * 32 + lane;
+      pf[d] = nidx < n ? __ldcg(s + nidx) : 0.0f;
+      if (b < nb) {
+        const uint32_t first = b == 0 ? 1u : 0u;  // element 0 seeds the fold
+        const uint32_t m = (uint32_t)umin64(32, n - b * 32);
+        if (first == 0 && m == 32) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, v, j));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float e = __shfl_sync(0xffffffffu, v, j);
+            if ((uint32_t)j >= first && (uint32_t)j < m) acc = __fadd_rn(acc, e);
+          }
+        }
+      }
+    }
+  }
+  return acc;
 }
 
+// A thread's strict left fold of s[0..n) seeded at s[0] (n >= 1), for short
+// folds where a warp per fold would leave most lanes idle.
+__device__ __forceinline__ float thread_serial_fold(const float* __restrict__ s, uint64_t n) {
+  float acc = s[0];
+  for (uint64_t i = 1; i < n; ++i) acc = __fadd_rn(acc, s[i]);
+  return acc;
+}
+
+constexpr int kSerialFoldThreads = 128;
+// folds at least this long get a warp each (warp_serial_fold), shorter ones a
+// thread each
+constexpr uint64_t kWarpFoldMin = 256;
+
+// One strict fold per unit u < units: unit u covers s = x + (u / per_row) *
+// row_stride + (u % per_row) * len, len elements.  WARP selects a warp per
+// unit, else a thread per unit.
+template <bool WARP>
+__global__ void __launch_bounds__(kSerialFoldThreads)
+    serial_folds_kernel(const float* __restrict__ x, uint64_t units, uint64_t per_row, uint64_t row_stride,
+                        uint64_t len, float* __restrict__ out) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint64_t u = WARP ? blockIdx.x * (uint64_t)(kSerialFoldThreads / 32) + (threadIdx.x >> 5)
+                          : blockIdx.x * (uint64_t)kSerialFoldThreads + threadIdx.x;
+  if (u >= units) return;
+  if (len == 0) {
+    if (!WARP || lane == 0) out[u] = 0.0f;
+    return;
+  }
+  const float* s = x + (u / per_row) * row_stride + (u % per_row) * len;
+  const float acc = WARP ? warp_serial_fold(s, len, lane) : thread_serial_fold(s, len);
+  if (!WARP || lane == 0) out[u] = canon(acc);
+}
+
+static void launch_serial_folds(const float* x, uint64_t units, uint64_t per_row, uint64_t row_stride, uint64_t len,
+                                float* out, cudaStream_t stream) {
+  if (units == 0) return;
+  if (len >= kWarpFoldMin) {
+    const uint64_t per_block = kSerialFoldThreads / 32;
+    serial_folds_kernel<true><<<(unsigned)((units + per_block - 1) / per_block), kSerialFoldThreads, 0, stream>>>(
+        x, units, per_row, row_stride, len, out);
+  } else {
+    serial_folds_kernel<false><<<(unsigned)((units + kSerialFoldThreads - 1) / kSerialFoldThreads),
+                                 kSerialFoldThreads, 0, stream>>>(x, units, per_row, row_stride, len, out);
+  }
+}
+
+// strict_sum (evaluate.rs:498-589): one fold per row, in order.
 void launch_strict_sum(const float* x, uint64_t rows, uint64_t count, float* out, cudaStream_t stream) {
-  unsigned threads = 128;
-  strict_sum_kernel<<<(unsigned)((rows + threads - 1) / threads), threads, 0, stream>>>(x, rows, count, out);
+  launch_serial_folds(x, rows, 1, count, count, out, stream);
 }
 
-// strict_partial_sums (evaluate.rs:612-747): one thread per partition.
-__global__ void partial_sums_kernel(const float* __restrict__ x, uint64_t rows, uint64_t count, uint64_t P,
-                                    uint64_t per, float* __restrict__ partials) {
-  uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (i >= rows * P) return;
-  uint64_t r = i / P, p = i % P;
-  if (per == 0) { partials[i] = 0.0f; return; }
-  const float* s = x + r * count + p * per;
-  float acc = s[0];
-  for (uint64_t j = 1; j < per; ++j) acc = __fadd_rn(acc, s[j]);
-  partials[i] = canon(acc);
-}
-
+// strict_partial_sums (evaluate.rs:612-747) then the strict fold of each row's
+// partials (strict_partitioned_sum, :749-832).
 void launch_partitioned_sum(const float* x, uint64_t rows, uint64_t count, uint64_t P, uint64_t per,
                             float* partials, float* out, cudaStream_t stream) {
-  unsigned threads = 128;
-  partial_sums_kernel<<<(unsigned)((rows * P + threads - 1) / threads), threads, 0, stream>>>(x, rows, count, P,
-                                                                                            per, partials);
+  launch_serial_folds(x, rows * P, P, count, per, partials, stream);
   launch_strict_sum(partials, rows, P, out, stream);
 }
 

@@ -16,6 +16,14 @@ honour, in the builder's vocabulary, for the crate to transcribe:
 * dtype dispatchability (f32; bf16 through the widening families);
 * the subgroup realization the grouped fold uses (width 32, f32, XOR
   shuffle butterfly);
+* the measured cost row ``saturated-parallel-fold-steps``
+  (``declare_measured_saturated_parallel_fold_steps``, builder.rs:1344-1375):
+  the fold steps the device retires at once when saturated, fitted from a
+  dispatch sweep of this library's three sum strategies with the work-span
+  model ``sum over stages of (encoder + max(work / P, depth) * step)`` the
+  reference's Metal row is fitted with (crates/tiler-build/src/
+  metal_declaration.rs:387-421).  Silence (no measurement) declares no row,
+  as the reference's cost rows do;
 * the payload provenance: nvcc, ``sm_100a``, the Makefile's flags, and the
   entry list of the library's own registry.
 """
@@ -98,7 +106,101 @@ def subgroup_rows(facts: dict | None = None) -> list:
     return [({"width": f["warp_size"], "element": "F32", "combine": "XorShuffle"}, "Supported")]
 
 
-def target_profile(facts: dict | None = None) -> dict:
+COST_ROW_KEY = "cost.saturated-parallel-fold-steps"  # CostRow::SaturatedParallelFoldSteps (rows.rs:399-406)
+
+
+def fit_work_span(cells: list) -> dict:
+    """Least-squares fit of the work-span model
+    ``seconds = sum over stages of (encoder + max(work / P, depth) * step)``.
+
+    ``cells``: [{"stages": [(work, depth), ...], "seconds": t}].  P is searched
+    on a fine logarithmic grid; for each P the model is linear in (encoder,
+    step), solved by least squares on relative residuals.  Returns P, encoder,
+    step and the RMS relative residual of the best fit."""
+    import numpy as np
+    t = np.array([c["seconds"] for c in cells], dtype=np.float64)
+    n_st = np.array([len(c["stages"]) for c in cells], dtype=np.float64)
+    best = None
+    for P in np.exp(np.linspace(np.log(16.0), np.log(1 << 22), 1200)):
+        span = np.array([sum(max(w / P, d) for w, d in c["stages"]) for c in cells], dtype=np.float64)
+        A = np.stack([n_st / t, span / t], axis=1)  # relative: model / t should be 1
+        coef, *_ = np.linalg.lstsq(A, np.ones_like(t), rcond=None)
+        if coef[0] < 0 or coef[1] <= 0:
+            continue
+        res = float(np.sqrt(np.mean((A @ coef - 1.0) ** 2)))
+        if best is None or res < best["residual"]:
+            best = {"parallel_steps": float(P), "encoder_s": float(coef[0]), "step_s": float(coef[1]),
+                    "residual": res}
+    if best is None:
+        raise ValueError("no admissible work-span fit (negative encoder or step at every P)")
+    return best
+
+
+def measure_fold_cells(fam, torch, repeats: int = 20) -> list:
+    """The dispatch sweep on the current device: strict serial sums (one
+    thread per row: work rows*count, depth count), partitioned sums (two
+    stages: the partials, then their strict fold) and the declared-grouping
+    sum (one stage: depth k*rounds + 5 + warp slots per round, then the
+    partials).  Inputs stay L2-resident (at most 64 MiB); each cell is the
+    mean of ``repeats`` back-to-back launches after a warm-up."""
+    dev = "cuda"
+    gen = torch.Generator(dev).manual_seed(11)
+    cells = []
+
+    def timed(fn):
+        # the repeats captured in one CUDA graph, so host call overhead leaves
+        # no gaps between the launches being timed
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            for _ in range(repeats):
+                fn()
+        graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / repeats
+
+    for rows, count in [(128, 256), (1024, 256), (8192, 256), (65536, 64), (262144, 64), (32, 4096), (512, 2048),
+                        (4096, 1024), (16384, 512), (16, 16384)]:
+        x = torch.rand(rows, count, device=dev, generator=gen)
+        cells.append({"strategy": "strict", "rows": rows, "count": count, "stages": [(rows * count, count)],
+                      "seconds": timed(lambda: fam.strict_sum_f32(x))})
+        for parts in (16, 64):
+            if count % parts == 0 and count // parts >= 4:
+                per = count // parts
+                cells.append({"strategy": "partitioned", "rows": rows, "count": count, "partitions": parts,
+                              "stages": [(rows * count, per), (rows * parts, parts)],
+                              "seconds": timed(lambda: fam.partitioned_sum_f32(x, parts, per))})
+        del x
+    for n in (1 << 16, 1 << 18, 1 << 20, 1 << 22, 1 << 24):
+        x = torch.rand(n, device=dev, generator=gen)
+        g = fam.plan_grouping(1, n)
+        ws = fam.grouped_workspace(1, g)
+        slots = g["threads"] // 32
+        depth = g["k"] * g["rounds"] + g["rounds"] * (5 + slots) + g["partitions"]
+        cells.append({"strategy": "grouped", "rows": 1, "count": n, "grouping": g, "stages": [(n, depth)],
+                      "seconds": timed(lambda: fam.sum_f32(x, g, ws))})
+        del x, ws
+    return cells
+
+
+def cost_rows(measured_steps: int | None = None) -> list:
+    """The cost rows this profile declares: the measured
+    saturated-parallel-fold-steps row when a measurement is given, otherwise
+    none (a cost row's silence states no preference)."""
+    if measured_steps is None:
+        return []
+    if measured_steps <= 0:
+        raise ValueError("a cost row value is positive")
+    return [(COST_ROW_KEY, int(measured_steps), "MeasuredEnvironment")]
+
+
+def target_profile(facts: dict | None = None, measured_fold_steps: int | None = None) -> dict:
     """The whole profile as data (declaration name -> rows)."""
     return {
         "key": PROFILE_KEY,
@@ -107,6 +209,7 @@ def target_profile(facts: dict | None = None) -> dict:
         "numerics": numerics_rows("f32"),
         "dtype_dispatchability": dtype_rows(),
         "subgroup_realization": subgroup_rows(facts),
+        "cost": cost_rows(measured_fold_steps),
     }
 
 
@@ -154,3 +257,19 @@ def payload_entries() -> list:
         sym = L.tiler_cuda_entry_symbol(i).decode()
         out.append({"entry_key": sym.split(".", 1)[1], "symbol": sym})
     return out
+
+
+if __name__ == "__main__":
+    # python -m tiler_b200.target_profile: the dispatch sweep and its fit on cuda:0
+    import json
+
+    import torch
+
+    from . import families
+
+    cells = measure_fold_cells(families, torch)
+    fit = fit_work_span(cells)
+    print(json.dumps({"device": torch.cuda.get_device_name(0), "fit": fit,
+                      "cost": cost_rows(round(fit["parallel_steps"])),
+                      "cells": [{k: v for k, v in c.items() if k != "stages"} | {"stages": c["stages"]}
+                                for c in cells]}))
