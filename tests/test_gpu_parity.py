@@ -525,7 +525,7 @@ def test_gather_full_config_is_bit_exact(fam):
     assert (e.value.position, e.value.value, e.value.extent) == (4000, -7, 128256)
 
 
-@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 1024), (384, 768, 512)])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 1024), (384, 768, 512), (512, 256, 192), (1024, 1280, 320)])
 def test_gemm_bf16_silu_matches_oracle(fam, oracle_lib, m, n, k):
     a = oracle_lib.f32_to_bf16(seeded_normal(m + k, m * k).reshape(m, k))
     b = oracle_lib.f32_to_bf16(seeded_normal(n + k, n * k).reshape(n, k) * 0.05)
@@ -582,8 +582,9 @@ def test_gemm_silu_epilogue_is_the_bf16_rounding_of_the_certified_silu(fam, orac
     bvals = np.zeros(cols, np.uint16)
     bvals[:keep.size] = keep
     k = 64
-    a = np.zeros((128, k), np.uint16)
-    a[np.arange(128), np.arange(128) % k] = oracle_lib.f32_to_bf16(np.ones(1, np.float32))[0]
+    m = 256  # rows 0 and 128: the first rows of both CTAs of a cta_group::2 pair
+    a = np.zeros((m, k), np.uint16)
+    a[np.arange(m), np.arange(m) % k] = oracle_lib.f32_to_bf16(np.ones(1, np.float32))[0]
     b = np.zeros((cols, k), np.uint16)
     b[:, 0] = bvals  # only row 0 of A (one-hot at column 0) picks column 0 of B
     at = cuda(a.view(np.int16)).view(torch.bfloat16)
@@ -595,6 +596,8 @@ def test_gemm_silu_epilogue_is_the_bf16_rounding_of_the_certified_silu(fam, orac
     want = want[0, :keep.size]
     bad = np.nonzero(got != want)[0]
     assert bad.size == 0, (bad[:5], keep[bad[:5]], got[bad[:5]], want[bad[:5]])
+    # row 128 is one-hot at column 0 as well
+    assert np.array_equal(c[128, :keep.size], want)
 
 
 def test_route_a_program_through_the_runtime_adapter(fam, oracle_lib):

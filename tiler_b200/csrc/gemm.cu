@@ -138,6 +138,84 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])    \
       : "r"(taddr))
 
+// One epilogue warp's share of a finished accumulator: TMEM lanes of its
+// quarter (32 rows, row_base in C), columns [col0, col0 + kBN/2) of the tile
+// starting at TMEM column tmem_tile, in 32x64 boxes: tcgen05.ld, SiLU (or the
+// plain bf16 rounding), swizzled staging, one TMA store per box, and the box
+// to every peer block when the all-gather is fused.
+__device__ __forceinline__ void gemm_epilogue_tile(uint32_t tmem_tile, uint32_t col0, uint32_t stage_u32, uint32_t lane,
+                                                   uint64_t row_base, uint64_t col_base, int epilogue,
+                                                   const CUtensorMap* tmap_c, const GemmPeers& peers, uint64_t ldp,
+                                                   tiler_cuda_status* st) {
+#pragma unroll 1
+  for (uint32_t box = col0; box < col0 + (uint32_t)kBN / 2; box += kEpiBoxCols) {
+    // the previous box's store has finished reading the staging buffer
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    __syncwarp();
+#pragma unroll 1
+    for (uint32_t half = 0; half < 2; ++half) {
+      uint32_t r[32];
+      const uint32_t taddr = tmem_tile + box + half * 32;
+      TMEM_LD32(taddr, r);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (epilogue == 1) {
+        uint32_t uncertain = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          bool certain;
+          const uint32_t bits = silu_bf16_fast(__uint_as_float(r[j]), &certain);
+          uncertain |= (certain ? 0u : 1u) << j;
+          r[j] = bits;
+        }
+        if (__any_sync(0xffffffffu, uncertain != 0)) {
+          // rare: reload the accumulators and certify the flagged ones
+          uint32_t x[32];
+          TMEM_LD32(taddr, x);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if ((uncertain >> j) & 1u) r[j] = silu_bf16_certified(__uint_as_float(x[j]), g_exp2_hi, st);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = f32_to_bf16(canon(__uint_as_float(r[j])));
+      }
+      // row `lane` of the box: 16-byte chunk c (of 8) at c ^ (row & 7)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t chunk = half * 4 + q;
+        const uint32_t off = lane * 128 + ((chunk ^ (lane & 7)) * 16);
+        asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stage_u32 + off),
+                     "r"(r[8 * q] | (r[8 * q + 1] << 16)), "r"(r[8 * q + 2] | (r[8 * q + 3] << 16)),
+                     "r"(r[8 * q + 4] | (r[8 * q + 5] << 16)), "r"(r[8 * q + 6] | (r[8 * q + 7] << 16))
+                     : "memory");
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+      const int32_t x = (int32_t)(col_base + box), y = (int32_t)row_base;
+      asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap_c),
+                   "r"(x), "r"(y), "r"(stage_u32)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    if (peers.count) {
+      // the box to each peer: 8 lanes per 128-byte row, 4 rows per step
+      const uint32_t c = lane & 7, rr = lane >> 3;
+      const uint64_t col = col_base + box + c * 8;
+#pragma unroll
+      for (uint32_t r0 = 0; r0 < 32; r0 += 4) {
+        const uint32_t r = r0 + rr;
+        const uint4 v = lds_u4(stage_u32 + r * 128 + ((c ^ (r & 7)) * 16));
+        const uint64_t row = row_base + r;
+        for (uint32_t q = 0; q < peers.count; ++q)
+          if (peers.block[q]) *reinterpret_cast<uint4*>(peers.block[q] + row * ldp + col) = v;
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                              const __grid_constant__ CUtensorMap tmap_c, uint32_t m_blocks, uint32_t n_blocks,
@@ -225,73 +303,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&B.tmem_full[buf], (local >> 1) & 1, st)) { *abort_flag = 1; break; }
       if (*abort_flag) break;
       tmem_fence_after();
-#pragma unroll 1
-      for (uint32_t box = col0; box < col0 + (uint32_t)kBN / 2; box += kEpiBoxCols) {
-        // the previous box's store has finished reading the staging buffer
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-        __syncwarp();
-#pragma unroll 1
-        for (uint32_t half = 0; half < 2; ++half) {
-          uint32_t r[32];
-          const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + buf * kBN + box + half * 32;
-          TMEM_LD32(taddr, r);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          if (epilogue == 1) {
-            uint32_t uncertain = 0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              bool certain;
-              const uint32_t bits = silu_bf16_fast(__uint_as_float(r[j]), &certain);
-              uncertain |= (certain ? 0u : 1u) << j;
-              r[j] = bits;
-            }
-            if (__any_sync(0xffffffffu, uncertain != 0)) {
-              // rare: reload the accumulators and certify the flagged ones
-              uint32_t x[32];
-              TMEM_LD32(taddr, x);
-              asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if ((uncertain >> j) & 1u) r[j] = silu_bf16_certified(__uint_as_float(x[j]), g_exp2_hi, st);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = f32_to_bf16(canon(__uint_as_float(r[j])));
-          }
-          // row `lane` of the box: 16-byte chunk c (of 8) at c ^ (row & 7)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t chunk = half * 4 + q;
-            const uint32_t off = lane * 128 + ((chunk ^ (lane & 7)) * 16);
-            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(stage_u32 + off),
-                         "r"(r[8 * q] | (r[8 * q + 1] << 16)), "r"(r[8 * q + 2] | (r[8 * q + 3] << 16)),
-                         "r"(r[8 * q + 4] | (r[8 * q + 5] << 16)), "r"(r[8 * q + 6] | (r[8 * q + 7] << 16))
-                         : "memory");
-          }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) {
-          const int32_t x = (int32_t)(nb * kBN + box), y = (int32_t)(mb * kBM + quarter * 32);
-          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(&tmap_c),
-                       "r"(x), "r"(y), "r"(stage_u32)
-                       : "memory");
-          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        }
-        if (peers.count) {
-          // the box to each peer: 8 lanes per 128-byte row, 4 rows per step
-          const uint32_t c = lane & 7, rr = lane >> 3;
-          const uint64_t col = (uint64_t)nb * kBN + box + c * 8;
-#pragma unroll
-          for (uint32_t r0 = 0; r0 < 32; r0 += 4) {
-            const uint32_t r = r0 + rr;
-            const uint4 v = lds_u4(stage_u32 + r * 128 + ((c ^ (r & 7)) * 16));
-            const uint64_t row = (uint64_t)mb * kBM + quarter * 32 + r;
-            for (uint32_t q = 0; q < peers.count; ++q)
-              if (peers.block[q]) *reinterpret_cast<uint4*>(peers.block[q] + row * ldp + col) = v;
-          }
-        }
-      }
+      gemm_epilogue_tile(tmem_base + ((quarter * 32) << 16) + buf * kBN, col0, stage_u32, lane,
+                         (uint64_t)mb * kBM + quarter * 32, (uint64_t)nb * kBN, epilogue, &tmap_c, peers, ldp, st);
       tmem_fence_before();
       mbar_arrive(&B.tmem_empty[buf]);
     }
@@ -304,6 +317,191 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tmem_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---- the CTA-pair form: cta_group::2, 256 x 256 tiles per cluster of two ----
+//
+// A cluster of two CTAs (on the two SMs of a TPC) computes one 256 x 256 tile:
+// CTA r holds rows [128 r, 128 r + 128) of the A tile and rows [128 r,
+// 128 r + 128) of the B tile (N-split) in its shared memory, and its TMEM
+// holds its 128 rows x 256 columns of the accumulator.  CTA 0's MMA thread
+// issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16), which reads
+// both CTAs' operands; each SM therefore loads 32 KB per K-step of 64 for the
+// same FLOPs that take 48 KB in the single-CTA form.  Both CTAs' TMA loads
+// complete on CTA 0's full barrier (plain tiled loads with the cta_group::2
+// barrier form, no multicast); CTA 0's commits arrive on both CTAs' empty and
+// accumulator-full barriers; every epilogue warp of both CTAs arrives on CTA
+// 0's accumulator-empty barrier.  All waits are bounded as in the single-CTA
+// kernel.
+constexpr int kPairStages = 6;
+constexpr int kPairTileBBytes = (kBN / 2) * kBK * 2;  // this CTA's half of the 256 B rows: 16 KB
+constexpr int kPairStageBytes = kTileABytes + kPairTileBBytes;
+constexpr uint32_t kIdescPair = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                                ((uint32_t)((2 * kBM) >> 4) << 24);
+
+struct PairBars {
+  uint64_t full[kPairStages];
+  uint64_t empty[kPairStages];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t kPairSmem = 1024 + (size_t)kPairStages * kPairStageBytes + (size_t)kGemmEpiWarps * kEpiStageBytes +
+                             sizeof(PairBars) + 64;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// the shared::cluster address of the same variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_u32(uint32_t saddr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr), "r"(bytes) : "memory");
+}
+// a tiled 2-D load into this CTA's shared memory whose bytes complete on the
+// barrier at `bar_cluster` (CTA 0's), without multicast
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t smem_dst, const void* tmap, int32_t x, int32_t y,
+                                                 uint32_t bar_cluster, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(bar_cluster), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(kIdescPair), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+// CTA 0's commit: the barrier at the same offset in both CTAs receives one arrival
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const __grid_constant__ CUtensorMap tmap_c, uint32_t m_blocks, uint32_t n_blocks,
+                          uint32_t k_blocks, int epilogue, tiler_cuda_status* st,
+                          const __grid_constant__ GemmPeers peers, uint64_t ldp) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = ((raw + 1023) & ~1023u) - raw;
+  uint8_t* tiles = smem_raw + pad;
+  uint8_t* epi_stage = tiles + (size_t)kPairStages * kPairStageBytes;  // 1024-byte aligned
+  PairBars& B = *reinterpret_cast<PairBars*>(epi_stage + (size_t)kGemmEpiWarps * kEpiStageBytes);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+  const uint32_t num_tiles = m_blocks * n_blocks;  // 256 x 256 tiles
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) { mbar_init(&B.full[s], 1); mbar_init(&B.empty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&B.tmem_full[s], 1); mbar_init(&B.tmem_empty[s], 2 * kGemmEpiWarps); }
+    B.abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&B.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tmem_fence_before();
+  cluster_sync_all();  // both CTAs' barriers are initialised before either signals the other
+  tmem_fence_after();
+  const uint32_t tmem_base = B.tmem_base;
+  volatile int* abort_flag = &B.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      uint64_t it = 0;
+      for (uint32_t tile = cluster; tile < num_tiles && !*abort_flag; tile += clusters) {
+        const uint32_t mb = tile % m_blocks, nb = tile / m_blocks;
+        for (uint32_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const uint32_t s = it % kPairStages;
+          const uint64_t use = it / kPairStages;
+          if (use > 0 && !mbar_wait(&B.empty[s], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
+          const uint32_t sa = smem_u32(tiles + (size_t)s * kPairStageBytes);
+          const uint32_t full0 = mapa_shared(smem_u32(&B.full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx_u32(smem_u32(&B.full[s]), 2 * kPairStageBytes);
+          tma_load_2d_pair(sa, &tmap_a, (int)(kb * kBK), (int)(mb * 2 * kBM + rank * kBM), full0, keep);
+          tma_load_2d_pair(sa + kTileABytes, &tmap_b, (int)(kb * kBK), (int)(nb * kBN + rank * (kBN / 2)), full0,
+                           keep);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      uint64_t it = 0;
+      uint32_t local = 0;
+      for (uint32_t tile = cluster; tile < num_tiles && !*abort_flag; tile += clusters, ++local) {
+        const uint32_t buf = local & 1;
+        const uint32_t use = local >> 1;
+        if (use > 0 && !mbar_wait(&B.tmem_empty[buf], (use - 1) & 1, st)) { *abort_flag = 1; break; }
+        tmem_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * kBN;
+        for (uint32_t kb = 0; kb < k_blocks; ++kb, ++it) {
+          const uint32_t s = it % kPairStages;
+          if (!mbar_wait(&B.full[s], (uint32_t)((it / kPairStages) & 1), st)) { *abort_flag = 1; break; }
+          tmem_fence_after();
+          const uint32_t sa = smem_u32(tiles + (size_t)s * kPairStageBytes);
+          const uint32_t sb = sa + kTileABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_bf16_pair(d_tmem, smem_desc_sw128(sa + kk * 32), smem_desc_sw128(sb + kk * 32), (kb | kk) != 0);
+          mma_commit_pair(&B.empty[s]);  // both CTAs' stage s is free once these MMAs have read it
+        }
+        if (*abort_flag) break;
+        mma_commit_pair(&B.tmem_full[buf]);  // both halves of the accumulator are complete
+      }
+    }
+  } else {
+    const uint32_t quarter = warp & 3;
+    const uint32_t col0 = ((warp - 2) / 4) * (kBN / 2);
+    const uint32_t stage_u32 = smem_u32(epi_stage + (size_t)(warp - 2) * kEpiStageBytes);
+    uint32_t local = 0;
+    for (uint32_t tile = cluster; tile < num_tiles; tile += clusters, ++local) {
+      const uint32_t mb = tile % m_blocks, nb = tile / m_blocks;
+      const uint32_t buf = local & 1;
+      if (!mbar_wait(&B.tmem_full[buf], (local >> 1) & 1, st)) { *abort_flag = 1; break; }
+      if (*abort_flag) break;
+      tmem_fence_after();
+      gemm_epilogue_tile(tmem_base + ((quarter * 32) << 16) + buf * kBN, col0, stage_u32, lane,
+                         (uint64_t)mb * 2 * kBM + rank * kBM + quarter * 32, (uint64_t)nb * kBN, epilogue, &tmap_c,
+                         peers, ldp, st);
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&B.tmem_empty[buf]), 0));
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (peers.count) __threadfence_system();
+  }
+  tmem_fence_before();
+  cluster_sync_all();  // no arrival or load of one CTA targets the other after this
+  if (warp == 1) {
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
                  : "memory");
   }
 }
@@ -332,7 +530,23 @@ int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t 
   if (!make_tmap_2d(&tcm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, c, n, m, ldc * 2, (uint32_t)kEpiBoxCols, 32,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return TILER_CUDA_DEVICE_ERROR;
-  const uint32_t mbk = (uint32_t)(m / kBM), nbk = (uint32_t)(n / kBN), kbk = (uint32_t)(k / kBK);
+  const uint32_t kbk = (uint32_t)(k / kBK);
+  static const int pair_env = [] {
+    const char* e = getenv("TILER_GEMM_PAIR");
+    return e ? atoi(e) : 1;
+  }();
+  if (pair_env && m % (2 * kBM) == 0 && sm_count >= 2) {
+    // the CTA-pair form: B's tensor map boxes are half the N rows of a tile
+    CUtensorMap tbp;
+    if (!make_tmap(&tbp, b, n, k, kBN / 2)) return TILER_CUDA_DEVICE_ERROR;
+    const uint32_t mb2 = (uint32_t)(m / (2 * kBM)), nbk2 = (uint32_t)(n / kBN);
+    const uint32_t grid = 2 * std::min<uint32_t>(mb2 * nbk2, (uint32_t)sm_count / 2);
+    cudaFuncSetAttribute(gemm_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
+    gemm_bf16_pair_kernel<<<grid, kGemmThreads, kPairSmem, stream>>>(ta, tbp, tcm, mb2, nbk2, kbk, epilogue, st,
+                                                                     peers, ldc);
+    return TILER_CUDA_OK;
+  }
+  const uint32_t mbk = (uint32_t)(m / kBM), nbk = (uint32_t)(n / kBN);
   const uint32_t tiles = mbk * nbk;
   const unsigned grid = std::min<uint32_t>(tiles, (uint32_t)sm_count);
   cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem);
