@@ -457,7 +457,8 @@ def test_quantize_refusals(fam):
 
 
 @pytest.mark.parametrize("dtype,rows,extent,chunk", [(torch.float32, 8192, 4096, 0), (torch.float32, 1000, 1024, 300),
-                                                    (torch.bfloat16, 777, 4096, 100)])
+                                                    (torch.bfloat16, 777, 4096, 100), (torch.float32, 17, 256, 0),
+                                                    (torch.bfloat16, 1000, 1024, 0)])
 def test_rms_norm_host_buffers_match_the_device_path(fam, dtype, rows, extent, chunk):
     # chunked upload / kernel / download gives the device path's bits, for a
     # broadcast weight row and for a per-row weight matrix
