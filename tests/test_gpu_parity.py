@@ -291,6 +291,34 @@ def test_softmax_with_a_mask_tensor_matches_oracle(fam, oracle_lib, rows, extent
     assert_bits_equal(got, want, "masked softmax")
 
 
+@pytest.mark.parametrize("extent", [1000, 2048])
+def test_softmax_mask_tensor_trailing_runs_match_oracle(fam, oracle_lib, extent):
+    """Mask rows ending in -inf runs of every length around the warp's scan
+    step (0 .. extent, the whole row included), a NaN mask entry, and x that
+    is NaN, +inf or -inf under a run (NaN and +inf poison the row)."""
+    tails = [0, 1, 3, 4, 5, 31, 32, 33, 127, 128, 129, 130, extent // 2, extent - 4, extent - 1, extent]
+    mask = seeded_normal(extent, len(tails) * extent).reshape(len(tails), extent)
+    for i, tl in enumerate(tails):
+        if tl:
+            mask[i, extent - tl:] = -np.inf
+    mask[2, 10] = -np.inf  # an interior -inf before a live entry
+    mask[4, extent - 6] = np.nan  # a NaN entry just before the run
+    rows = 4 * len(tails)
+    x = seeded_normal(extent + 7, rows * extent).reshape(rows, extent) * 3
+    for i, tl in enumerate(tails):
+        if tl:
+            x[len(tails) + i, extent - 1] = np.nan
+            x[2 * len(tails) + i, extent - tl] = np.inf
+            x[3 * len(tails) + i, extent - 1] = -np.inf
+    got = host(fam.softmax_masked(cuda(x), cuda(mask)))
+    with np.errstate(invalid="ignore"):
+        t = x + mask[np.arange(rows) % len(tails)]
+    t[np.isnan(t)] = np.array([0x7FC00000], np.uint32).view(np.float32)[0]
+    st, want = oracle_lib.softmax_f32(t, nthreads=8)
+    assert st == 0
+    assert_bits_equal(got, want, f"masked softmax trailing runs, extent {extent}")
+
+
 def test_softmax_causal_mask_tensor_equals_the_in_kernel_mask(fam):
     # the 0 / -inf block-causal mask as a tensor gives the in-kernel mask's bits,
     # poisoned rows (NaN or +inf under the mask) included
