@@ -12,8 +12,7 @@
  *   - the registered operation families evaluated by tiler-reference
  *     (crates/tiler-reference/src/lib.rs:86-110).
  * Each export below names the reference interface it stands in for.  A Rust
- * `tiler-cuda` crate binds these with `extern "C"` declarations (see
- * INTEGRATION.md).
+ * `tiler-cuda` crate binds these with `extern "C"` declarations.
  *
  * Conventions (mirroring RoutedBinding, crates/tiler-runtime/src/load/
  * route.rs:145-191):

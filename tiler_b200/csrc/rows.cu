@@ -273,10 +273,6 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
   __syncthreads();
   volatile int* abort_flag = &SS.abort;
   if (nwaves == 0) return;
-#ifdef TILER_RMS_PROBE_TL
-  unsigned long long* tl = reinterpret_cast<unsigned long long*>(st) + 64 + blockIdx.x * 8;
-  if (threadIdx.x == 0) tl[0] = global_ns();
-#endif
 
   if (pwarp < kRmsLoadWarps) {
     // ---- producers -----------------------------------------------------------
@@ -300,9 +296,6 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
         if (lane < wr) bulk_g2s(&S.stage[stage][lane * kRmsPitch], gbase + lane * row_bytes, bytes, &S.full[stage], keep);
       }
     }
-#ifdef TILER_RMS_PROBE_TL
-    if (threadIdx.x == 0) tl[5] = global_ns();
-#endif
   } else if (pwarp == kRmsLoadWarps) {
     // ---- chain warp ------------------------------------------------------------
     bool signalled = false;
@@ -315,7 +308,6 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
         if (!mbar_wait(&S.full[stage], (uint32_t)((i / kRmsStages) & 1), st)) *abort_flag = 1;
         if (*abort_flag) break;
         const uint32_t nvec = (uint32_t)umin64(kRmsSlabBytes, row_bytes - c * kRmsSlabBytes) / 16;
-#ifndef TILER_RMS_PROBE_NO_CHAIN
         if (lane < wr) {
           const uint32_t rowp = smem_u32(&S.stage[stage][lane * kRmsPitch]);
           uint32_t v = 0;
@@ -329,7 +321,6 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
           }
           acc = rms_fold_vectors<E>(acc, rowp, v, nvec);
         }
-#endif
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&S.empty[stage]);
@@ -344,9 +335,6 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
       const uint64_t use = wv >> 1;
       if (use > 0 && !mbar_wait(&S.scale_empty[slot], (uint32_t)((use - 1) & 1), st)) { *abort_flag = 1; break; }
       if (lane < wr) S.scale[slot][lane] = s;
-#ifdef TILER_RMS_PROBE_TL
-      if (lane == 0 && wv < 2) tl[1 + wv] = global_ns();
-#endif
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.scale_full[slot]);
     }
@@ -361,7 +349,6 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
       const uint32_t slot = wv & 1;
       if (!mbar_wait(&S.scale_full[slot], (uint32_t)((wv >> 1) & 1), st)) *abort_flag = 1;
       if (*abort_flag) break;
-#ifndef TILER_RMS_PROBE_SKIP_NORMALIZE
       for (uint32_t r = nw; r < wr; r += kRmsNormWarps) {
         const float s = S.scale[slot][r];
         const uint64_t row = rb + wave_first_row(wv) + r;
@@ -476,11 +463,7 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
           }
         }
       }
-#endif
       __syncwarp();
-#ifdef TILER_RMS_PROBE_TL
-      if (lane == 0 && wv < 2) atomicMax(&tl[3 + wv], global_ns());
-#endif
       if (lane == 0) mbar_arrive(&S.scale_empty[slot]);
     }
   }
@@ -647,16 +630,10 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
   if (threadIdx.x < kSmxMaxGroup) mbar_init(&full[threadIdx.x], 1);
   fence_barrier_init();
   __syncthreads();
-#ifdef TILER_SMX_PROBE_SPAN
-  const uint64_t span_t0 = global_ns();
-#endif
 
   for (uint64_t g = 0; g < ngroups; ++g) {
     const uint64_t row0 = group_row0(g);
     const uint32_t n = (uint32_t)umin64(G, rows - row0);
-#ifdef TILER_SMX_PROBE_TIMES
-    const long long t0 = clock64();
-#endif
     // each row warp loads its own row; its previous bulk store must have
     // finished reading the buffer first
     bool ok = true;
@@ -668,9 +645,6 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
       }
       ok = mbar_wait(&full[warp], (uint32_t)(g & 1), st);
     }
-#ifdef TILER_SMX_PROBE_TIMES
-    const long long t1 = clock64();
-#endif
 
     if (!chain_warp && warp < n) {
       // ---- max and exponentials for row `warp` ---------------------------------
@@ -801,9 +775,6 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
       if (lane == 0 && !chain_warp) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
       return;
     }
-#ifdef TILER_SMX_PROBE_TIMES
-    long long t2 = clock64();
-#endif
 
     if (chain_warp) {
       // ---- chain warp: lane r folds row r's denominator ------------------------
@@ -841,9 +812,6 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
       }
     }
     __syncthreads();
-#ifdef TILER_SMX_PROBE_TIMES
-    long long t3 = clock64();
-#endif
 
     if (!chain_warp && warp < n) {
       // ---- out = e * r (softmax.rs:306-312), written in place, then one bulk store
@@ -873,25 +841,6 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
       }
     }
     // no barrier here: a row warp reloads only its own buffer, after its store
-#ifdef TILER_SMX_PROBE_TIMES
-    long long t4 = clock64();
-#endif
-#ifdef TILER_SMX_PROBE_SPAN
-    if (threadIdx.x == 0 && g + 1 == ngroups) {
-      uint64_t* T = reinterpret_cast<uint64_t*>(st) + 8;
-      uint32_t smid;
-      asm("mov.u32 %0, %%smid;" : "=r"(smid));
-      T[blockIdx.x * 3] = span_t0; T[blockIdx.x * 3 + 1] = global_ns(); T[blockIdx.x * 3 + 2] = smid;
-    }
-#endif
-#ifdef TILER_SMX_PROBE_TIMES
-    if (threadIdx.x == 0) {  // phase cycles summed over all groups (probe scratch after the status word)
-      unsigned long long* T = reinterpret_cast<unsigned long long*>(st) + 8;
-      atomicAdd(&T[0], (unsigned long long)(t1 - t0)); atomicAdd(&T[1], (unsigned long long)(t2 - t1));
-      atomicAdd(&T[2], (unsigned long long)(t3 - t2)); atomicAdd(&T[3], (unsigned long long)(t4 - t3));
-      atomicAdd(&T[4], 1ull);
-    }
-#endif
   }
   if (lane == 0 && !chain_warp) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // stores complete
 }
