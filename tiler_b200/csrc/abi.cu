@@ -90,7 +90,7 @@ int32_t validate_grouping(uint64_t rows, uint64_t count, const tiler_cuda_groupi
       return TILER_CUDA_INVALID_APPLICATION;
     if ((uint64_t)g->combine_rounds * (g->combine_threads / 32 + 1) > kMaxSlotFloats) return TILER_CUDA_UNSUPPORTED;
   }
-  if (rows * g->partitions > 0x7fffffffull) return TILER_CUDA_SHAPE_TOO_LARGE;
+  if (rows && g->partitions > 0x7fffffffull / rows) return TILER_CUDA_SHAPE_TOO_LARGE;
   if (g->partitions > 1) {
     if (!workspace) return TILER_CUDA_INVALID_APPLICATION;
     if (workspace_bytes < tiler_cuda_grouped_workspace_bytes(rows, g)) return TILER_CUDA_WORKSPACE_TOO_SMALL;

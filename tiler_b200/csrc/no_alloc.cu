@@ -17,6 +17,7 @@
 // other.  The tickets are cleared on every call; the partials are always
 // written before they are read.
 #include "common.cuh"
+#include "drv.cuh"
 #include "kernels.h"
 
 namespace tc {
@@ -29,19 +30,33 @@ static __device__ __align__(256) uint8_t g_no_alloc_scratch[kNoAllocScratchBytes
 
 namespace {
 std::mutex g_no_alloc_mutex;
-void* g_no_alloc_ptr[64] = {};
+struct NoAllocSlot {
+  CUcontext owner = nullptr;  // the context the address was taken in
+  void* ptr = nullptr;
+};
+NoAllocSlot g_no_alloc_slot[64];
 
-// Device address of g_no_alloc_scratch on the current device (set up once).
+// Device address of g_no_alloc_scratch on the current device.  It is taken
+// once per device and taken again if the device's context was replaced (after
+// cudaDeviceReset the module, and with it the array, is loaded anew).
 int32_t no_alloc_scratch(void** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return TILER_CUDA_DEVICE_ERROR;
+  typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+  static CtxGetCurrentFn ctx_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  if (!ctx_current) return TILER_CUDA_DEVICE_ERROR;
+  CUcontext cur = nullptr;
+  if (ctx_current(&cur) != CUDA_SUCCESS) return TILER_CUDA_DEVICE_ERROR;
   std::lock_guard<std::mutex> lock(g_no_alloc_mutex);
-  if (!g_no_alloc_ptr[dev]) {
+  NoAllocSlot& slot = g_no_alloc_slot[dev];
+  if (!slot.ptr || slot.owner != cur) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_no_alloc_scratch) != cudaSuccess || !p) return TILER_CUDA_DEVICE_ERROR;
-    g_no_alloc_ptr[dev] = p;
+    if (ctx_current(&cur) != CUDA_SUCCESS) return TILER_CUDA_DEVICE_ERROR;  // the runtime may have made it
+    slot.ptr = p;
+    slot.owner = cur;
   }
-  *out = g_no_alloc_ptr[dev];
+  *out = slot.ptr;
   return TILER_CUDA_OK;
 }
 }  // namespace
@@ -52,12 +67,16 @@ extern "C" int32_t tiler_cuda_sum_f32_no_alloc(tiler_cuda_context* ctx, void* st
                                                uint64_t count, const tiler_cuda_grouping* g, float* out) {
   using namespace tc;
   if (!ctx || !g) return TILER_CUDA_INVALID_APPLICATION;
-  if (rows > kNoAllocMaxRows || rows * g->partitions > kNoAllocMaxPartials) return TILER_CUDA_SHAPE_TOO_LARGE;
+  if (rows > kNoAllocMaxRows || (rows && g->partitions > kNoAllocMaxPartials / rows)) return TILER_CUDA_SHAPE_TOO_LARGE;
   if (rows == 0 || count == 0 || g->partitions <= 1)
     return tiler_cuda_sum_f32(ctx, stream, x, rows, count, g, nullptr, 0, out);
+  if (!x || !out) return TILER_CUDA_INVALID_APPLICATION;
   if (!bind(ctx)) return TILER_CUDA_DEVICE_ERROR;
   void* scratch = nullptr;
   int32_t r = no_alloc_scratch(&scratch);
+  if (r != TILER_CUDA_OK) return r;
+  // every refusal happens before the shared array is touched
+  r = validate_grouping(rows, count, g, kNoAllocScratchBytes, scratch);
   if (r != TILER_CUDA_OK) return r;
   const uint64_t partial_bytes = (rows * g->partitions * 4 + 255) / 256 * 256;
   // The tickets must start at zero; a memset allocates nothing.
