@@ -1,9 +1,17 @@
-"""Two-GPU parity of the fused GEMM + all-gather (one process per GPU, NCCL).
+"""Multi-GPU parity of the sharded families (one process per GPU, NCCL).
 
-Runs only where two GPUs are visible; the single-GPU suite skips it.  The
-fused form (the all-gather done by peer stores from the GEMM epilogue) must
-give the same blocks, bit for bit, as the local GEMM followed by an NCCL
-all-gather.
+Runs at every world size in {2, 4, 8} that the box's GPUs allow; a 1-GPU box
+skips it.  Each world checks, on every rank:
+
+* the fused GEMM + all-gather (peer stores from the GEMM epilogue) against the
+  local GEMM followed by an NCCL all-gather, bit for bit, on two calls in a
+  row with different operands, each result read before the next call;
+* row-sharded RMS norm and causal softmax (rank r owns ``row_range``; the
+  softmax shard passes its global first row as ``row_offset``) against the
+  same family run over all rows on one GPU, bit for bit;
+* the rank-ordered sum (per-shard grid groupings, partials all-gathered over
+  NCCL and folded strictly in rank order) against the oracle's evaluation of
+  that declared grouping.
 """
 import os
 import socket
@@ -23,6 +31,66 @@ def _free_port():
     return p
 
 
+def _checks(rank, world):
+    import numpy as np
+
+    import oracle
+    from tiler_b200 import families as fam, sharding
+    results = {}
+    gen = torch.Generator("cuda").manual_seed(4)  # the same operands on every rank
+
+    # fused GEMM + all-gather, two calls in a row with different A
+    m, n, k = 1024, 256 * world * 2, 512
+    w = (torch.randn(n, k, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    c0, c1 = sharding.row_range(n, rank, world)
+    ws = w[c0:c1].contiguous()
+    blocks = sharding.PeerBlocks(torch.full((world, m, c1 - c0), -1.0, device="cuda", dtype=torch.bfloat16),
+                                 fam.ipc_export, fam.ipc_open, fam.ipc_close)
+    ok = True
+    for call in range(2):
+        a = (torch.randn(m, k, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+        want = sharding.gemm_n_sharded(a, ws, lambda aa, ww: fam.gemm_bf16(aa, ww, "silu"), assemble=False)
+        got = sharding.gemm_n_sharded_fused(
+            a, ws, blocks, lambda aa, ww, p, r, nw: fam.gemm_bf16_allgather(aa, ww, p, r, nw, "silu"))
+        ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))  # read before the next call
+    torch.distributed.barrier()
+    blocks.close()
+    results["gemm_fused_allgather"] = bool(ok)
+
+    # row-sharded RMS norm [8192, 4096] f32
+    x = torch.randn(8192, 4096, device="cuda", generator=gen)
+    wr = torch.rand(4096, device="cuda", generator=gen) + 0.5
+    full = fam.rms_norm(x, wr)
+    r0, r1 = sharding.row_range(8192, rank, world)
+    part = fam.rms_norm(x[r0:r1].contiguous(), wr)
+    results["rms_row_shard"] = bool(torch.equal(part.view(torch.int32), full[r0:r1].view(torch.int32)))
+    del x, full, part
+
+    # row-sharded causal softmax [8192, 2048] (shards start inside mask blocks at W = 8)
+    z = torch.randn(8192, 2048, device="cuda", generator=gen) * 3
+    full = fam.softmax(z, causal_period=2048)
+    part = fam.softmax(z[r0:r1].contiguous(), causal_period=2048,
+                       row_offset=sharding.causal_row_offset(8192, rank, world))
+    results["softmax_row_shard"] = bool(torch.equal(part.view(torch.int32), full[r0:r1].view(torch.int32)))
+    del z, full, part
+
+    # the rank-ordered sum of 2^24 contributors
+    count = 1 << 24
+    s = torch.rand(count, device="cuda", generator=gen) * 2 - 1
+    s0, s1 = sharding.row_range(count, rank, world)
+    shard = s[s0:s1].contiguous()
+    got = sharding.sum_across_ranks(shard, lambda t: fam.sum_f32(t, fam.plan_grouping(1, t.numel())))
+    host = s.cpu().numpy()
+    partials = []
+    for q in range(world):
+        q0, q1 = sharding.row_range(count, q, world)
+        _, v = oracle.grid_fold(host[q0:q1], fam.plan_grouping(1, q1 - q0))
+        partials.append(np.float32(np.asarray(v).ravel()[0]))
+    want = sharding._strict_fold(np.array(partials, np.float32))
+    results["sum_rank_ordered"] = bool(np.float32(got).view(np.uint32) == np.float32(want).view(np.uint32))
+    return results
+
+
 def _worker(rank, world, port, q):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -30,42 +98,28 @@ def _worker(rank, world, port, q):
     torch.cuda.set_device(rank)
     import torch.distributed as dist
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
-    from tiler_b200 import families as fam, sharding
     try:
-        m, n, k = 1024, 2048, 512
-        gen = torch.Generator("cuda").manual_seed(4)  # the same operands on every rank
-        a = (torch.randn(m, k, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
-        w = (torch.randn(n, k, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
-        c0, c1 = sharding.row_range(n, rank, world)
-        ws = w[c0:c1].contiguous()
-        want = sharding.gemm_n_sharded(a, ws, lambda aa, ww: fam.gemm_bf16(aa, ww, "silu"), assemble=False)
-        blocks = sharding.PeerBlocks(torch.full((world, m, c1 - c0), -1.0, device="cuda", dtype=torch.bfloat16),
-                                     fam.ipc_export, fam.ipc_open, fam.ipc_close)
-        ok = True
-        for _ in range(3):  # repeated launches into the same buffers
-            got = sharding.gemm_n_sharded_fused(
-                a, ws, blocks, lambda aa, ww, p, r, nw: fam.gemm_bf16_allgather(aa, ww, p, r, nw, "silu"))
-            torch.cuda.synchronize()
-            ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))
-        dist.barrier()
-        blocks.close()
-        q.put((rank, bool(ok)))
-    except Exception as exc:  # report instead of leaving the peer waiting
+        q.put((rank, _checks(rank, world)))
+    except Exception as exc:  # report instead of leaving the peers waiting
         q.put((rank, repr(exc)))
         raise
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_gemm_allgather_equals_gemm_then_nccl_allgather():
-    world, port = 2, _free_port()
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_families_match_one_gpu(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = sorted(q.get(timeout=300) for _ in range(world))
+    results = sorted((q.get(timeout=600) for _ in range(world)), key=lambda t: t[0])
     for p in procs:
         p.join(timeout=120)
-    assert results == [(0, True), (1, True)], results
+    want = {"gemm_fused_allgather": True, "rms_row_shard": True, "softmax_row_shard": True,
+            "sum_rank_ordered": True}
+    assert results == [(r, want) for r in range(world)], results

@@ -108,10 +108,16 @@ class PeerBlocks:
 def gemm_n_sharded_fused(a: torch.Tensor, w_shard: torch.Tensor, blocks: PeerBlocks, fused_gemm, group=None):
     """The contraction's multi-GPU form with the exchange fused into the GEMM:
     ``fused_gemm(a, w_shard, ptrs, rank, world)`` writes this rank's columns
-    into every rank's block buffer; a one-element all-reduce on the stream then
-    orders every rank's kernel before anyone reads.  Returns the local
-    [world, m, n/world] blocks (the layout ``gemm_n_sharded(assemble=False)``
-    returns)."""
+    into every rank's block buffer.  Two one-element all-reduces on the stream
+    order the exchange: the one before the launch holds every rank's kernel
+    until all ranks have reached this call, so no rank overwrites a peer's
+    blocks while that peer still reads the previous call's result (reads the
+    caller enqueued on this stream before the call); the one after orders every
+    rank's kernel before anyone reads.  Returns the local [world, m, n/world]
+    blocks (the layout ``gemm_n_sharded(assemble=False)`` returns); they stay
+    valid until this rank's next call."""
+    ready = torch.zeros(1, device=a.device)
+    dist.all_reduce(ready, group=group)
     fused_gemm(a, w_shard, blocks.ptrs, blocks.rank, blocks.world)
     done = torch.zeros(1, device=a.device)
     dist.all_reduce(done, group=group)
