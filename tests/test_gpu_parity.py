@@ -235,6 +235,86 @@ def test_rms_norm_bf16_matches_oracle(fam, oracle_lib, rows, extent):
     assert (got == want).all(), f"{(got != want).sum()} bf16 mismatches"
 
 
+def _fold_stress_rows(seed, rows, extent):
+    """Rows that drive the warp-cooperative strict fold of the squares through
+    every event it has: binade crossings from tiny first squares, exact ties
+    (coarse value grids), running values below 2^-103 (folded one at a time),
+    overflow to +inf, NaN and inf inputs, all-zero and subnormal rows."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, extent)).astype(np.float32)
+    for r in range(rows):
+        kind = r % 14
+        v = x[r]
+        if kind == 1:
+            v[:] = np.round(v * 8) / 8  # squares on a coarse grid: ties
+        elif kind == 2:
+            v[:] = np.round(v * 64) / 64
+        elif kind == 3:
+            v[:] = np.ldexp(v, -60)  # running value near 2^-103..2^-120
+        elif kind == 4:
+            v[:] = np.ldexp(v, -75)  # squares underflow toward subnormals
+        elif kind == 5:
+            v[:] = np.ldexp(v, 62)  # the fold overflows to +inf
+        elif kind == 6:
+            v[0] = 1e-30  # the fold starts tiny, then jumps
+        elif kind == 7:
+            v[:] = 0.0
+        elif kind == 8:
+            v[rng.integers(extent)] = np.nan
+        elif kind == 9:
+            v[rng.integers(extent)] = np.inf
+        elif kind == 10:
+            v[:] = np.ldexp(v, rng.integers(-40, 40, extent)).astype(np.float32)
+        elif kind == 11:
+            v[:] = np.sqrt(rng.integers(0, 4096, extent)).astype(np.float32)
+        elif kind == 12:
+            v[:] = np.ldexp(np.float32(1.0), -140) * rng.integers(1, 64, extent)  # subnormal inputs
+        elif kind == 13:
+            v[rng.integers(extent)] = np.inf
+            v[rng.integers(extent)] = np.nan
+    return x
+
+
+@pytest.mark.parametrize("extent", [4096, 4092, 1000, 260, 8])
+def test_rms_norm_f32_fold_stress_rows_match_oracle(fam, oracle_lib, extent):
+    rows = 14 * 9
+    x = _fold_stress_rows(extent, rows, extent)
+    w = seeded_uniform(6, extent, 0.5, 1.5)
+    got = host(fam.rms_norm(cuda(x), cuda(w)))
+    st, want = oracle_lib.rms_norm_f32(x, w, nthreads=8)
+    assert st == 0
+    assert_bits_equal(got, want, f"rms f32 stress {extent}")
+
+
+@pytest.mark.parametrize("extent", [4096, 8192, 1000, 8])
+def test_rms_norm_bf16_fold_stress_rows_match_oracle(fam, oracle_lib, extent):
+    rows = 14 * 9
+    x = oracle_lib.f32_to_bf16(_fold_stress_rows(extent + 1, rows, extent))
+    w = oracle_lib.f32_to_bf16(seeded_uniform(8, extent, 0.5, 1.5))
+    xt = cuda(x.view(np.int16)).view(torch.bfloat16)
+    wt = cuda(w.view(np.int16)).view(torch.bfloat16)
+    got = host(fam.rms_norm(xt, wt).view(torch.int16)).view(np.uint16)
+    st, want = oracle_lib.rms_norm_bf16(x, w, nthreads=8)
+    assert st == 0
+    bad = np.argwhere(got != want)
+    assert bad.size == 0, f"{len(bad)} mismatches, first {bad[:4].tolist()}"
+
+
+def test_rms_norm_quantize_fusion_fold_stress_rows(fam, oracle_lib):
+    extent = 4096
+    x = _fold_stress_rows(99, 14 * 4, extent)
+    keep = [r for r in range(x.shape[0]) if r % 14 not in (4, 5, 7, 8, 9, 12, 13)]  # rows the quantize refuses
+    x = np.ascontiguousarray(x[keep])
+    w = seeded_uniform(5, extent, 0.5, 1.5)
+    st, y = oracle_lib.rms_norm_f32(x, w, nthreads=8)
+    st, wc, ws, _ = oracle_lib.quantize_i8_rows(y, nthreads=8)
+    if st != 0:
+        pytest.skip("stress rows outside the quantize domain")
+    codes, scales = fam.rms_norm_quantize_i8(cuda(x), cuda(w))
+    assert (host(codes) == wc).all()
+    assert_bits_equal(host(scales), ws)
+
+
 def test_rms_norm_bf16_special_values_match_oracle(fam, oracle_lib):
     # rows whose outputs are NaN (NaN or inf input), overflow to inf (huge
     # weight), fall to bf16 subnormals (one huge and many tiny inputs), are

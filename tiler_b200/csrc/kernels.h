@@ -40,6 +40,12 @@ int launch_softmax(const float* x, uint64_t rows, uint64_t extent, uint64_t caus
 int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
                                 uint64_t extent, float eps, int8_t* codes, float* scales, tiler_cuda_status* st,
                                 int sm_count, cudaStream_t stream);
+// rms_scan.cu: the warp-per-row RMS kernel (and its fused int8 quantize form);
+// false when the operands do not fit it (per-row weights, rows over 16 KB or
+// not a multiple of 16 bytes, unaligned pointers): the caller takes another form.
+bool rms_scan_launch(int bf16, int quant, const void* x, const void* w, int64_t w_row_stride, uint64_t rows,
+                     uint64_t extent, float eps, void* y, int8_t* codes, float* scales, tiler_cuda_status* st,
+                     int sm_count, cudaStream_t stream);
 void launch_bounded_wait_selftest(tiler_cuda_status* st, uint64_t limit_ns, cudaStream_t stream);
 void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
                              tiler_cuda_status* st, int sm_count, cudaStream_t stream);

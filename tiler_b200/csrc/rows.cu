@@ -502,6 +502,16 @@ __global__ void rms_norm_generic_kernel(const void* __restrict__ xv, const void*
   }
 }
 
+// TILER_RMS_FORM=wave in the environment (read once per process) selects the
+// wave kernel above for every shape; it is how the two forms are compared.
+static bool rms_wave_form_forced() {
+  static const bool forced = [] {
+    const char* v = getenv("TILER_RMS_FORM");
+    return v && strcmp(v, "wave") == 0;
+  }();
+  return forced;
+}
+
 int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
                                 uint64_t extent, float eps, int8_t* codes, float* scales, tiler_cuda_status* st,
                                 int sm_count, cudaStream_t stream) {
@@ -509,6 +519,9 @@ int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_st
   const bool aligned = ((uintptr_t)x % 16 == 0) && ((uintptr_t)w % 16 == 0) && ((uintptr_t)codes % 4 == 0) &&
                        extent % 4 == 0;
   if (!aligned) return TILER_CUDA_UNSUPPORTED;
+  if (!rms_wave_form_forced() &&
+      rms_scan_launch(0, 1, x, w, w_row_stride, rows, extent, eps, nullptr, codes, scales, st, sm_count, stream))
+    return 0;
   const uint64_t grid = umin64((uint64_t)sm_count, rows);
   cudaFuncSetAttribute(rms_norm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
   rms_norm_kernel<false, true><<<(unsigned)grid, kRmsThreads, kRmsSmemBytes, stream>>>(
@@ -532,7 +545,11 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
       rms_norm_generic_kernel<false><<<blocks, wpb * 32, 0, stream>>>(x, w, w_row_stride, rows, extent, eps, y);
     return 0;
   }
-  // One CTA per SM; each takes rows/grid consecutive rows in waves.
+  // The warp-per-row form where it applies (broadcast weights, rows up to 16 KB)
+  if (!rms_wave_form_forced() &&
+      rms_scan_launch(bf16, 0, x, w, w_row_stride, rows, extent, eps, y, nullptr, nullptr, st, sm_count, stream))
+    return 0;
+  // Otherwise one CTA per SM; each takes rows/grid consecutive rows in waves.
   const uint64_t grid = umin64((uint64_t)sm_count, rows);
   const uint32_t wave = (uint32_t)kRmsWave;
   if (bf16) {

@@ -3,6 +3,7 @@
 // the families are compiled together rather than with relocatable device code.
 #include "reduce.cu"
 #include "rows.cu"
+#include "rms_scan.cu"
 #include "maps.cu"
 #include "gemm.cu"
 #include "abi.cu"
