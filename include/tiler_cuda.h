@@ -144,6 +144,29 @@ const char* tiler_cuda_entry_symbol(uint32_t index);
 int32_t tiler_cuda_entry_query(const tiler_cuda_context* ctx, const char* symbol,
                                tiler_cuda_entry_props* out);
 
+/* ---- payload code (PayloadContent.code, crates/tiler-artifact/src/program/
+ * codec/payload.rs:228-424; validate_payload / prepare_entries /
+ * observe_prepared_entry, crates/tiler-runtime/src/adapter.rs:639-657) ----
+ * `code` is the artifact's code bytes: an sm_100a cubin built from this
+ * library's kernel sources (tiler_b200/tiler_kernels.cubin).  Loading checks
+ * that it is an image the device accepts and that it carries this C-ABI's
+ * version; anything else is TILER_CUDA_PAYLOAD_REFUSED.  A module bound to a
+ * context runs, for every launch on that context, the kernels it carries
+ * (RMS norm f32 / bf16 / fused quantize, grouped sum and maximum) in place of
+ * the library's built-in copies; unbind with NULL.  Unload only after unbinding
+ * it from every context and after its launches have finished. */
+typedef struct tiler_cuda_module tiler_cuda_module;
+int32_t tiler_cuda_module_load(tiler_cuda_context* ctx, const void* code, uint64_t code_bytes,
+                               tiler_cuda_module** out);
+/* observe_prepared_entry for a module: TILER_CUDA_PAYLOAD_REFUSED when the
+ * module does not carry the entry's kernel. */
+int32_t tiler_cuda_module_entry(const tiler_cuda_module* module, const char* symbol,
+                                tiler_cuda_entry_props* out);
+int32_t tiler_cuda_context_bind_module(tiler_cuda_context* ctx, tiler_cuda_module* module);
+/* Launches made from the module so far (evidence that its code is what ran). */
+int32_t tiler_cuda_module_launch_count(const tiler_cuda_module* module, uint64_t* out);
+int32_t tiler_cuda_module_unload(tiler_cuda_module* module);
+
 /* ---- status word and completion (dispatch completion, adapter.rs:675-677) */
 int32_t tiler_cuda_status_reset(void* stream, tiler_cuda_status* status_dev);
 int32_t tiler_cuda_status_fetch(void* stream, const tiler_cuda_status* status_dev,

@@ -12,6 +12,8 @@ import threading
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libtiler_cuda.so")
+# The payload code a plan artifact carries: the same kernels as an sm_100a cubin.
+CUBIN_PATH = os.path.join(HERE, "tiler_kernels.cubin")
 
 OK = 0
 INVALID_APPLICATION = 1
@@ -77,6 +79,11 @@ SIGNATURES = {
     "tiler_cuda_entry_count": (u32, []),
     "tiler_cuda_entry_symbol": (C.c_char_p, [u32]),
     "tiler_cuda_entry_query": (i32, [P, C.c_char_p, C.POINTER(EntryProps)]),
+    "tiler_cuda_module_load": (i32, [P, C.c_char_p, u64, C.POINTER(P)]),
+    "tiler_cuda_module_entry": (i32, [P, C.c_char_p, C.POINTER(EntryProps)]),
+    "tiler_cuda_context_bind_module": (i32, [P, P]),
+    "tiler_cuda_module_launch_count": (i32, [P, C.POINTER(u64)]),
+    "tiler_cuda_module_unload": (i32, [P]),
     "tiler_cuda_status_reset": (i32, [P, P]),
     "tiler_cuda_status_fetch": (i32, [P, P, C.POINTER(Error)]),
     "tiler_cuda_status_decode": (i32, [C.POINTER(Status), C.POINTER(Error)]),

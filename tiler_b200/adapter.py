@@ -66,6 +66,10 @@ class Payload:
     subgroup_width: int
     entries: tuple
     provenance: dict = field(default_factory=dict)
+    # PayloadContent.code: the compiled code bytes (an sm_100a cubin of this
+    # library's kernels, tiler_b200/tiler_kernels.cubin), or None to run the
+    # library's built-in copies
+    code: bytes | None = None
 
 
 @dataclass
@@ -100,6 +104,7 @@ class CudaRuntimeAdapter:
         self.facts = None
         self.trace: list = []
         self.committed = False
+        self.module = None  # the loaded payload code (tiler_cuda_module*)
 
     # ---- pre-commit phases (may refuse) ------------------------------------
     def bind_execution_context(self):
@@ -129,6 +134,12 @@ class CudaRuntimeAdapter:
         if st != N.OK:
             which = payload.entries[refused.value].symbol if refused.value < len(payload.entries) else ""
             raise Refusal("validate_payload", st, which)
+        if payload.code is not None:
+            handle = C.c_void_p()
+            st = self.native.tiler_cuda_module_load(self.ctx, payload.code, len(payload.code), C.byref(handle))
+            if st != N.OK:
+                raise Refusal("validate_payload", st, "payload code")
+            self.module = handle.value
 
     def observe_live_device(self) -> dict:
         self.trace.append("observe_live_device")
@@ -139,7 +150,10 @@ class CudaRuntimeAdapter:
         prepared = {}
         for e in payload.entries:
             props = N.EntryProps()
-            st = self.native.tiler_cuda_entry_query(self.ctx, e.symbol.encode(), C.byref(props))
+            if self.module is not None:  # the entry as the payload's own code carries it
+                st = self.native.tiler_cuda_module_entry(self.module, e.symbol.encode(), C.byref(props))
+            else:
+                st = self.native.tiler_cuda_entry_query(self.ctx, e.symbol.encode(), C.byref(props))
             if st != N.OK:
                 raise Refusal("prepare_entries", st, e.symbol)
             prepared[e.entry_key] = PreparedEntry(e, {k: int(getattr(props, k)) for k, _ in props._fields_})
@@ -167,17 +181,44 @@ class CudaRuntimeAdapter:
     def dispatch(self, prepared: dict, plan: DispatchPlan, workspace) -> list:
         self.trace.append("dispatch")
         results = []
-        for ln in plan.launches:
-            entry = prepared[ln.entry_key].entry
-            run = (self.executor or _default_executor)(entry.symbol)
-            try:
-                results.append(run(ln.args))
-            except Exception as exc:  # no fallback after the commit
-                code = getattr(exc, "code", N.DEVICE_ERROR)
-                raise Failure("dispatch", code, f"{entry.symbol}: {exc}") from exc
+        # the payload's code is bound to the context the executor launches on
+        # for the duration of the dispatch
+        exec_ctx = None
+        if self.module is not None and self.executor is None:
+            from . import families as F
+            exec_ctx = F.context(self.device)
+            st = self.native.tiler_cuda_context_bind_module(exec_ctx, self.module)
+            if st != N.OK:
+                raise Failure("dispatch", st, "binding the payload code")
+        try:
+            for ln in plan.launches:
+                entry = prepared[ln.entry_key].entry
+                run = (self.executor or _default_executor)(entry.symbol)
+                try:
+                    results.append(run(ln.args))
+                except Exception as exc:  # no fallback after the commit
+                    code = getattr(exc, "code", N.DEVICE_ERROR)
+                    raise Failure("dispatch", code, f"{entry.symbol}: {exc}") from exc
+        finally:
+            if exec_ctx is not None:
+                self.native.tiler_cuda_context_bind_module(exec_ctx, None)
         return results
 
+    def module_launches(self) -> int:
+        """Launches that ran from the payload's own code so far."""
+        if self.module is None:
+            return 0
+        n = C.c_uint64()
+        self.native.tiler_cuda_module_launch_count(self.module, C.byref(n))
+        return int(n.value)
+
     def close(self):
+        if self.module is not None and self.native is not None:
+            import torch
+            if torch.cuda.is_available():
+                torch.cuda.synchronize(self.device)  # its launches have finished
+            self.native.tiler_cuda_module_unload(self.module)
+            self.module = None
         if self.ctx is not None and self.native is not None:
             self.native.tiler_cuda_context_destroy(self.ctx)
             self.ctx = None

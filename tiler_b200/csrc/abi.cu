@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 struct tiler_cuda_context {
   int device;
@@ -18,6 +19,7 @@ struct tiler_cuda_context {
   // copy streams and events of the host-buffer entry points (made on first use)
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   cudaEvent_t ev[2 * 32 + 2] = {};
+  tiler_cuda_module* module = nullptr;  // bound payload module (launches run its kernels)
 };
 
 namespace {
@@ -29,32 +31,46 @@ std::vector<bool> g_table_ready;
 
 // 2^(j/256) as a double-double (hi + lo, |error| < 2^-106), computed in
 // binary128 and written once per device into g_exp2_table.
+struct Exp2Table {
+  double pairs[256][2];
+  double hi[256];
+};
+
+const Exp2Table& exp2_table_host() {
+  static const Exp2Table t = [] {
+    Exp2Table e;
+    for (int j = 0; j < 256; ++j) {
+      __float128 v = exp2q((__float128)j / 256);
+      double hi = (double)v;
+      e.pairs[j][0] = hi;
+      e.pairs[j][1] = (double)(v - (__float128)hi);
+      e.hi[j] = hi;
+    }
+    return e;
+  }();
+  return t;
+}
+
 int init_exp_table(int device) {
   std::lock_guard<std::mutex> lock(g_init_mutex);
   if ((int)g_table_ready.size() <= device) g_table_ready.resize(device + 1, false);
   if (g_table_ready[device]) return TILER_CUDA_OK;
-  double host[256][2];
-  for (int j = 0; j < 256; ++j) {
-    __float128 v = exp2q((__float128)j / 256);
-    double hi = (double)v;
-    double lo = (double)(v - (__float128)hi);
-    host[j][0] = hi;
-    host[j][1] = lo;
-  }
-  if (cudaMemcpyToSymbol(g_exp2_table, host, sizeof(host)) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
-  double hi_col[256];
-  for (int j = 0; j < 256; ++j) hi_col[j] = host[j][0];
-  if (cudaMemcpyToSymbol(g_exp2_hi, hi_col, sizeof(hi_col)) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
+  const Exp2Table& t = exp2_table_host();
+  if (cudaMemcpyToSymbol(g_exp2_table, t.pairs, sizeof(t.pairs)) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
+  if (cudaMemcpyToSymbol(g_exp2_hi, t.hi, sizeof(t.hi)) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;
   g_table_ready[device] = true;
   return TILER_CUDA_OK;
 }
 
 int32_t last_error_status() {
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? TILER_CUDA_OK : TILER_CUDA_DEVICE_ERROR;
+  const bool module_failed = tl_module_launch_failed;
+  tl_module_launch_failed = false;
+  return e == cudaSuccess && !module_failed ? TILER_CUDA_OK : TILER_CUDA_DEVICE_ERROR;
 }
 
 bool bind(const tiler_cuda_context* ctx) {
+  tl_module = ctx->module;
   int cur = -1;
   cudaGetDevice(&cur);
   if (cur != ctx->device) return cudaSetDevice(ctx->device) == cudaSuccess;
@@ -105,19 +121,21 @@ struct Entry {
   const void* func;
   int threads;
   size_t smem;
+  const char* kernel = nullptr;  // C name of the kernel a payload module carries for it (or none)
 };
 
 const Entry kEntries[] = {
-    {"tiler_cuda.sum_f32.grouped", (const void*)grouped_fold_kernel<0, 4>, 512, 0},
-    {"tiler_cuda.max_f32.grouped", (const void*)grouped_fold_kernel<1, 4>, 512, 0},
+    {"tiler_cuda.sum_f32.grouped", (const void*)tiler_grouped_sum_k4, 512, 0, "tiler_grouped_sum_k4"},
+    {"tiler_cuda.max_f32.grouped", (const void*)tiler_grouped_max_k4, 512, 0, "tiler_grouped_max_k4"},
     {"tiler_cuda.sum_f32.strict", (const void*)serial_folds_kernel<true>, kSerialFoldThreads, 0},
     {"tiler_cuda.sum_f32.partitioned", (const void*)serial_folds_kernel<false>, kSerialFoldThreads, 0},
     {"tiler_cuda.sum_f32.cooperative", (const void*)cooperative_sum_kernel, 1024, 0},
-    {"tiler_cuda.rms_norm_f32", (const void*)rms_norm_kernel<false>, kRmsThreads, kRmsSmemBytes},
-    {"tiler_cuda.rms_norm_bf16", (const void*)rms_norm_kernel<true>, kRmsThreads, kRmsSmemBytes},
+    {"tiler_cuda.rms_norm_f32", (const void*)tiler_rms_norm_f32, kRsThreads, kRsSmemBytes, "tiler_rms_norm_f32"},
+    {"tiler_cuda.rms_norm_bf16", (const void*)tiler_rms_norm_bf16, kRsThreads, kRsSmemBytes, "tiler_rms_norm_bf16"},
     {"tiler_cuda.softmax_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.quantize_i8_rows", (const void*)quantize_i8_rows_kernel, kQThreads, 0},
-    {"tiler_cuda.rms_norm_quantize_i8", (const void*)rms_norm_kernel<false, true>, kRmsThreads, kRmsSmemBytes},
+    {"tiler_cuda.rms_norm_quantize_i8", (const void*)tiler_rms_norm_quantize_i8, kRsThreads, kRsSmemBytes,
+     "tiler_rms_norm_quantize_i8"},
     {"tiler_cuda.softmax_masked_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.dequantize_i8_rows", (const void*)dequantize_i8_rows_kernel, 256, 0},
     {"tiler_cuda.quantize_affine_u8", (const void*)quantize_affine_u8_kernel, 256, 0},
@@ -249,6 +267,101 @@ int32_t tiler_cuda_entry_query(const tiler_cuda_context* ctx, const char* symbol
   out->threads_per_block = e->threads;
   out->pad = 0;
   return TILER_CUDA_OK;
+}
+
+// ---- payload code: load, prepare, bind ----------------------------------------
+
+int32_t tiler_cuda_module_load(tiler_cuda_context* ctx, const void* code, uint64_t code_bytes,
+                               tiler_cuda_module** out) {
+  if (out) *out = nullptr;
+  CHECK_CTX(ctx);
+  if (!out || !code) return TILER_CUDA_INVALID_APPLICATION;
+  // an ELF image (a cubin); anything else is refused before the driver sees it
+  if (code_bytes < 64 || memcmp(code, "\x7f" "ELF", 4) != 0) return TILER_CUDA_PAYLOAD_REFUSED;
+  const ModuleDriver& d = module_driver();
+  if (!d.ok) return TILER_CUDA_DEVICE_ERROR;
+  if (cudaFree(nullptr) != cudaSuccess) return TILER_CUDA_DEVICE_ERROR;  // the device's context is current
+  CUcontext cur = nullptr;
+  if (d.ctx_current(&cur) != CUDA_SUCCESS || !cur) return TILER_CUDA_DEVICE_ERROR;
+  CUmodule mod = nullptr;
+  // code for another architecture, or not a loadable image: refused
+  if (d.load(&mod, code) != CUDA_SUCCESS) return TILER_CUDA_PAYLOAD_REFUSED;
+  auto refuse = [&](int32_t st) {
+    d.unload(mod);
+    return st;
+  };
+  // provenance: the module was built from this library's sources, for this C-ABI
+  CUdeviceptr abi_ptr = 0;
+  size_t abi_size = 0;
+  uint32_t abi = 0;
+  if (d.get_global(&abi_ptr, &abi_size, mod, "tiler_cuda_payload_abi") != CUDA_SUCCESS || abi_size != 4 ||
+      d.memcpy_dtoh(&abi, abi_ptr, 4) != CUDA_SUCCESS || abi != TILER_CUDA_ABI_VERSION)
+    return refuse(TILER_CUDA_PAYLOAD_REFUSED);
+  // the module's own copy of the certified-exp table
+  const Exp2Table& t = exp2_table_host();
+  CUdeviceptr tp = 0, hp = 0;
+  size_t tsz = 0, hsz = 0;
+  if (d.get_global(&tp, &tsz, mod, "g_exp2_table") == CUDA_SUCCESS && tsz == sizeof(t.pairs) &&
+      d.memcpy_htod(tp, t.pairs, sizeof(t.pairs)) != CUDA_SUCCESS)
+    return refuse(TILER_CUDA_DEVICE_ERROR);
+  if (d.get_global(&hp, &hsz, mod, "g_exp2_hi") == CUDA_SUCCESS && hsz == sizeof(t.hi) &&
+      d.memcpy_htod(hp, t.hi, sizeof(t.hi)) != CUDA_SUCCESS)
+    return refuse(TILER_CUDA_DEVICE_ERROR);
+  auto* m = new tiler_cuda_module();
+  m->device = ctx->device;
+  m->cu_ctx = cur;
+  m->mod = mod;
+  for (int i = 0; i < kModuleKernelCount; ++i) {
+    CUfunction f = nullptr;
+    m->fn[i] = d.get_function(&f, mod, kModuleKernels[i]) == CUDA_SUCCESS ? f : nullptr;
+    m->smem_allowed[i] = 48 * 1024;
+  }
+  *out = m;
+  return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_module_entry(const tiler_cuda_module* m, const char* symbol, tiler_cuda_entry_props* out) {
+  if (!m || !out) return TILER_CUDA_INVALID_APPLICATION;
+  const Entry* e = find_entry(symbol);
+  if (!e) return TILER_CUDA_INVALID_APPLICATION;
+  const int i = e->kernel ? module_kernel_index(e->kernel) : -1;
+  if (i < 0 || !m->fn[i]) return TILER_CUDA_PAYLOAD_REFUSED;  // the module does not carry this entry
+  const ModuleDriver& d = module_driver();
+  int regs = 0, maxt = 0, ssmem = 0;
+  if (d.func_get_attribute(&regs, CU_FUNC_ATTRIBUTE_NUM_REGS, m->fn[i]) != CUDA_SUCCESS ||
+      d.func_get_attribute(&maxt, CU_FUNC_ATTRIBUTE_MAX_THREADS_PER_BLOCK, m->fn[i]) != CUDA_SUCCESS ||
+      d.func_get_attribute(&ssmem, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, m->fn[i]) != CUDA_SUCCESS)
+    return TILER_CUDA_DEVICE_ERROR;
+  out->num_regs = regs;
+  out->max_threads_per_block = maxt;
+  out->static_smem_bytes = ssmem;
+  out->dynamic_smem_bytes = (int64_t)e->smem;
+  out->threads_per_block = e->threads;
+  out->pad = 0;
+  return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_context_bind_module(tiler_cuda_context* ctx, tiler_cuda_module* m) {
+  if (!ctx) return TILER_CUDA_INVALID_APPLICATION;
+  if (m && m->device != ctx->device) return TILER_CUDA_INVALID_APPLICATION;
+  ctx->module = m;
+  if (!m) tl_module = nullptr;
+  return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_module_launch_count(const tiler_cuda_module* m, uint64_t* out) {
+  if (!m || !out) return TILER_CUDA_INVALID_APPLICATION;
+  *out = m->launches.load();
+  return TILER_CUDA_OK;
+}
+
+int32_t tiler_cuda_module_unload(tiler_cuda_module* m) {
+  if (!m) return TILER_CUDA_OK;
+  if (tl_module == m) tl_module = nullptr;
+  const ModuleDriver& d = module_driver();
+  const CUresult r = d.unload(m->mod);
+  delete m;
+  return r == CUDA_SUCCESS ? TILER_CUDA_OK : TILER_CUDA_DEVICE_ERROR;
 }
 
 int32_t tiler_cuda_status_reset(void* stream, tiler_cuda_status* status_dev) {

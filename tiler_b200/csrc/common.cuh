@@ -81,8 +81,14 @@ __device__ __forceinline__ void report_undecided(tiler_cuda_status* s) {
 // host runtime (abi.cu, from __float128 exp2q) into g_exp2_table; the fast
 // path reads its hi column from a shared-memory copy.
 
+// C names, so a payload module's copies are found by name (cuModuleGetGlobal)
+// and written the same way when the module is loaded.
+extern "C" {
 __device__ double g_exp2_table[256][2];
 __device__ double g_exp2_hi[256];  // the hi column again, contiguous (read where no shared copy is kept)
+// The C-ABI version the code was built for: a payload module must carry it.
+__device__ uint32_t tiler_cuda_payload_abi = TILER_CUDA_ABI_VERSION;
+}
 
 // 256/ln2 and ln2/256 split so that n*kLn2By256Hi is exact for |n| < 2^17.
 constexpr double kInvLn2x256 = 369.3299304675746271;            // 256 / ln 2 (rounded)

@@ -18,6 +18,7 @@
 // loads issued before the folds consume them.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace tc {
 
@@ -147,10 +148,9 @@ __device__ float compose_block_generic(const float* seq, uint64_t n, uint32_t T,
 }
 
 template <int OP, int K>
-__global__ void __launch_bounds__(1024) grouped_fold_kernel(const float* __restrict__ x, uint64_t count,
-                                                            GroupedParams gp, float* __restrict__ partials,
-                                                            unsigned int* __restrict__ tickets,
-                                                            float* __restrict__ out) {
+__device__ __forceinline__ void grouped_fold(const float* __restrict__ x, uint64_t count, GroupedParams gp,
+                                             float* __restrict__ partials, unsigned int* __restrict__ tickets,
+                                             float* __restrict__ out) {
   extern __shared__ float slots[];
   const uint64_t P = gp.partitions;
   const uint64_t row = blockIdx.x / P, p = blockIdx.x % P;
@@ -189,6 +189,24 @@ __global__ void __launch_bounds__(1024) grouped_fold_kernel(const float* __restr
   }
 }
 
+}  // namespace tc
+
+#define TILER_GROUPED_KERNEL(NAME, OP, K)                                                                   \
+  extern "C" __global__ void __launch_bounds__(1024)                                                       \
+      NAME(const float* __restrict__ x, uint64_t count, tc::GroupedParams gp, float* __restrict__ partials, \
+           unsigned int* __restrict__ tickets, float* __restrict__ out) {                                  \
+    tc::grouped_fold<OP, K>(x, count, gp, partials, tickets, out);                                         \
+  }
+TILER_GROUPED_KERNEL(tiler_grouped_sum_k1, 0, 1)
+TILER_GROUPED_KERNEL(tiler_grouped_sum_k2, 0, 2)
+TILER_GROUPED_KERNEL(tiler_grouped_sum_k4, 0, 4)
+TILER_GROUPED_KERNEL(tiler_grouped_max_k1, 1, 1)
+TILER_GROUPED_KERNEL(tiler_grouped_max_k2, 1, 2)
+TILER_GROUPED_KERNEL(tiler_grouped_max_k4, 1, 4)
+#undef TILER_GROUPED_KERNEL
+
+namespace tc {
+
 void launch_grouped_fold(int op, const float* x, uint64_t rows, uint64_t count, const GroupedParams& gp,
                          float* partials, unsigned int* tickets, float* out, cudaStream_t stream) {
   const uint32_t G = gp.threads / 32;
@@ -197,21 +215,15 @@ void launch_grouped_fold(int op, const float* x, uint64_t rows, uint64_t count, 
   uint32_t cG = gp.combine_threads / 32;
   size_t smem = sizeof(float) * (size_t)std::max<uint64_t>((uint64_t)R * G + R, (uint64_t)cR * cG + cR);
   dim3 grid((unsigned)(rows * gp.partitions));
-  if (op == 0) {
-    if (gp.k == 4)
-      grouped_fold_kernel<0, 4><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
-    else if (gp.k == 2)
-      grouped_fold_kernel<0, 2><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
-    else
-      grouped_fold_kernel<0, 1><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
-  } else {
-    if (gp.k == 4)
-      grouped_fold_kernel<1, 4><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
-    else if (gp.k == 2)
-      grouped_fold_kernel<1, 2><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
-    else
-      grouped_fold_kernel<1, 1><<<grid, gp.threads, smem, stream>>>(x, count, gp, partials, tickets, out);
-  }
+  const int ki = gp.k == 4 ? 2 : gp.k == 2 ? 1 : 0;
+  static const void* const fns[2][3] = {{(const void*)tiler_grouped_sum_k1, (const void*)tiler_grouped_sum_k2,
+                                         (const void*)tiler_grouped_sum_k4},
+                                        {(const void*)tiler_grouped_max_k1, (const void*)tiler_grouped_max_k2,
+                                         (const void*)tiler_grouped_max_k4}};
+  static const char* const names[2][3] = {{"tiler_grouped_sum_k1", "tiler_grouped_sum_k2", "tiler_grouped_sum_k4"},
+                                          {"tiler_grouped_max_k1", "tiler_grouped_max_k2", "tiler_grouped_max_k4"}};
+  launch_kernel(fns[op][ki], names[op][ki], grid, dim3(gp.threads), smem, stream, x, count, gp, partials, tickets,
+                out);
 }
 
 // ---- reference-vocabulary groupings ------------------------------------------
