@@ -344,19 +344,26 @@ def family_suite(fam, torch, world, steps_small, warmup):
     # quantize / decode f32 [16384, 4096]
     xq = [torch.randn(16384, 4096, device=dev, generator=gen) for _ in range(2)]
     codes, scales = fam.quantize_i8_rows(xq[0])
-    ms = time_device(lambda i: fam.quantize_i8_rows(xq[i % 2], check=False), steps_small, warmup, world, graph=True)
+    # outputs rotate over 3 x 64 MB so the codes do not stay in L2 between steps
+    qout = [(torch.empty_like(codes), torch.empty_like(scales)) for _ in range(3)]
+    ms = time_device(lambda i: fam.quantize_i8_rows(xq[i % 2], check=False, out=qout[i % 3]), steps_small * 3,
+                     warmup, world, graph=True)
     qbytes = 16384 * 4096 * 5 + 16384 * 4
-    rec("quantize_i8_16384x4096", "GB/s", qbytes, ms, steps_small, hbm)
+    rec("quantize_i8_16384x4096", "GB/s", qbytes, ms, steps_small * 3, hbm)
+    del qout
     yq = torch.empty(16384, 4096, device=dev)
     cd = torch.empty_like(codes)
 
     # fused RMS norm -> int8 quantize over the RMS config (x read once, y never written)
-    xr = torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=gen)
+    xr = [torch.randn(RMS_ROWS, RMS_EXTENT, device=dev, generator=gen) for _ in range(2)]
     wr_ = torch.rand(RMS_EXTENT, device=dev, generator=gen) + 0.5
-    ms = time_device(lambda i: fam.rms_norm_quantize_i8(xr, wr_, check=False), steps_small, warmup, world, graph=True)
+    fout = [(torch.empty(RMS_ROWS, RMS_EXTENT, device=dev, dtype=torch.int8), torch.empty(RMS_ROWS, device=dev))
+            for _ in range(4)]
+    ms = time_device(lambda i: fam.rms_norm_quantize_i8(xr[i % 2], wr_, check=False, out=fout[i % 4]),
+                     steps_small * 4, warmup, world, graph=True)
     rec("rms_norm_quantize_i8_8192x4096", "GB/s", RMS_ROWS * RMS_EXTENT * 5 + RMS_EXTENT * 4 + RMS_ROWS * 4, ms,
-        steps_small, hbm)
-    del xr
+        steps_small * 4, hbm)
+    del xr, fout
 
     def run_dec(i):
         L.tiler_cuda_dequantize_i8_rows(ctx, cur_stream(), None, codes.data_ptr(), scales.data_ptr(), 16384, 4096,
@@ -368,9 +375,11 @@ def family_suite(fam, torch, world, steps_small, warmup):
     # gather: ids i32 [8192] from bf16 table [128256, 4096]
     table = (torch.randn(128256, 4096, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
     idss = [torch.randint(0, 128256, (8192,), device=dev, dtype=torch.int32, generator=gen) for _ in range(8)]
-    ga = torch.empty(8192, 4096, device=dev, dtype=torch.bfloat16)
-    ms = time_device(lambda i: fam.gather_rows(table, idss[i % 8], out=ga, check=False), steps_small * 4, warmup,
-                     world, graph=True)
+    # outputs rotate over 4 x 64 MB so the rows written do not stay in L2 between steps
+    gas = [torch.empty(8192, 4096, device=dev, dtype=torch.bfloat16) for _ in range(4)]
+    ga = gas[0]
+    ms = time_device(lambda i: fam.gather_rows(table, idss[i % 8], out=gas[i % 4], check=False), steps_small * 4,
+                     warmup, world, graph=True)
     rec("gather_bf16_8192_of_128256x4096", "GB/s", 8192 * 4 + 8192 * 4096 * 4, ms, steps_small * 4, hbm)
 
     # bf16 contraction [8192,4096] x [4096,14336] + SiLU (W stored [N,K])
@@ -417,8 +426,80 @@ def family_suite(fam, torch, world, steps_small, warmup):
                 rec("gemm_bf16_silu_nsharded_fused_allgather", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps,
                     tflops * world)
                 blocks.close()
-    del table, ga, wt, cc
+    del table, ga, gas, wt, cc
     torch.cuda.empty_cache()
+    out.update(strong_scaled_suite(fam, torch, world, steps_small, warmup))
+    return out
+
+
+def strong_scaled_suite(fam, torch, world, steps_small, warmup):
+    """The row families and the sum split over the ranks (strong scaling: the
+    whole job is the one BASELINE config; rank r takes sharding.row_range of
+    its rows).  `value` is the whole job's algorithmic bytes over the max over
+    ranks of the device time, so the driver's per-N values give the
+    strong-scaling efficiency directly; `us_per_launch` shows the floor that
+    launch latency sets once a shard is small."""
+    import ctypes as C
+
+    from tiler_b200 import _native as N
+    from tiler_b200 import sharding
+    hbm, _, _ = measured_peaks()
+    rank = torch.distributed.get_rank() if world > 1 else 0
+    gen = torch.Generator("cuda").manual_seed(11)
+    dev = "cuda"
+    out = {}
+
+    def rec(name, total_bytes, ms, steps, shard):
+        v = total_bytes * steps / (ms / 1e3) / 1e9
+        out[name] = {"value": round(v, 2), "unit": "GB/s", "frac_per_gpu": round(v / world / hbm, 4),
+                     "us_per_launch": round(ms * 1e3 / steps, 2), "scaling": "strong", "shard": shard}
+
+    # RMS f32: rows [r0, r1) of the [8192, 4096] batch
+    r0, r1 = sharding.row_range(RMS_ROWS, rank, world)
+    shard_bytes = (r1 - r0) * RMS_EXTENT * 4
+    nb = max(3, -(-3 * 126 * 2 ** 20 // (2 * shard_bytes)))  # rotation well past L2
+    xs = [torch.randn(r1 - r0, RMS_EXTENT, device=dev, generator=gen) for _ in range(nb)]
+    ys = [torch.empty_like(xs[0]) for _ in range(nb)]
+    w = torch.rand(RMS_EXTENT, device=dev, generator=gen) + 0.5
+    steps = steps_small * 8
+    ms = time_device(lambda i: fam.rms_norm(xs[i % nb], w, out=ys[i % nb], check=False), steps, warmup, world,
+                     graph=True)
+    rec("strong_rms_norm_f32_8192x4096", RMS_BYTES, ms, steps, f"{r1 - r0} rows per rank")
+    del xs, ys
+
+    # causal softmax: rows [r0, r1) of [65536, 2048]; the shard keeps its global row offset
+    r0, r1 = sharding.row_range(65536, rank, world)
+    nb = 2 if world > 1 else 1
+    zs = [torch.randn(r1 - r0, 2048, device=dev, generator=gen) * 3 for _ in range(nb)]
+    zo = [torch.empty_like(zs[0]) for _ in range(nb)]
+    ms = time_device(lambda i: fam.softmax(zs[i % nb], causal_period=2048, row_offset=r0, out=zo[i % nb],
+                                           check=False), steps_small * 2, warmup, world, graph=True)
+    rec("strong_softmax_f32_65536x2048_causal", 65536 * 2048 * 8, ms, steps_small * 2, f"{r1 - r0} rows per rank")
+    del zs, zo
+
+    # the sum of 2^24: each rank's shard under its grid grouping, the W partials
+    # all-gathered over NCCL and folded strictly in rank order on the device
+    n = 1 << 24
+    s0, s1 = sharding.row_range(n, rank, world)
+    shards = [torch.rand(s1 - s0, device=dev, generator=gen) * 2 - 1 for _ in range(4)]
+    g = fam.plan_grouping(1, s1 - s0)
+    gs = N.Grouping.from_dict(g)
+    ws = fam.grouped_workspace(1, g)
+    part = torch.empty(1, device=dev)
+    gathered = torch.empty(world, device=dev)
+    total = torch.empty(1, device=dev)
+    ctx, L = fam.context(), N.lib()
+
+    def run_sum(i):
+        L.tiler_cuda_sum_f32(ctx, cur_stream(), shards[i % 4].data_ptr(), 1, s1 - s0, C.byref(gs), ws.data_ptr(),
+                             ws.numel(), part.data_ptr())
+        if world > 1:
+            torch.distributed.all_gather_into_tensor(gathered, part)
+            L.tiler_cuda_strict_sum_f32(ctx, cur_stream(), gathered.data_ptr(), 1, world, total.data_ptr())
+    steps = steps_small * 8
+    ms = time_device(run_sum, steps, warmup, world)
+    rec("strong_sum_f32_2^24_rank_ordered", n * 4, ms, steps, f"{s1 - s0} contributors per rank")
+    del shards
     return out
 
 

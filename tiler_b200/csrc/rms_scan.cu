@@ -141,35 +141,48 @@ __device__ __forceinline__ void rms_norm_scan(const uint8_t* __restrict__ x, con
 
     // ---- the strict fold of the squares -------------------------------------
     NonnegFold F = fold_start(TILER_RS_SERIAL);
-    bool x_finite = true;
+    float vn[8];  // the next chunk, loaded a chunk ahead
+    rs_load8<BF16>(base, 0, lane, vn);
     for (uint32_t c = 0; c < nchunks; ++c) {
       float v[8], a[8];
-      rs_load8<BF16>(base, c, lane, v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = vn[i];
+      if (c + 1 < nchunks) rs_load8<BF16>(base, c + 1, lane, vn);
       const bool tail = (c + 1) * 256 > extent;
 #pragma unroll
       for (int i = 0; i < 8; i += 2) mul2(v[i], v[i + 1], v[i], v[i + 1], a[i], a[i + 1]);
+      if (tail) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        if (tail && c * 256 + 8 * lane + i >= extent) a[i] = 0.0f;  // past the row's end
-        x_finite &= isfinite(a[i]);
+        for (int i = 0; i < 8; ++i)
+          if (c * 256 + 8 * lane + i >= extent) a[i] = 0.0f;  // past the row's end
       }
       fold_chunk(F, a, lane);
     }
-    x_finite = __all_sync(0xffffffffu, x_finite);
     const float total = fold_value(F);
     const float mean = __fdiv_rn(total, (float)extent);
     const float s = rsqrt_cr(__fadd_rn(mean, eps));
-    // w, x * s finite and w * (x * s) free of 0 * inf: no NaN can arise
-    const bool plain = w_finite && x_finite && isfinite(s);
+    // A finite total means every square, so every x, is finite; then with w
+    // finite, x * s finite and w * (x * s) free of 0 * inf: no NaN can arise.
+    const bool plain = w_finite && isfinite(total) && isfinite(s);
 
     if constexpr (!QUANT) {
       // ---- y = w * (x * s) ------------------------------------------------------
       uint8_t* yr = y + row * row_bytes;
+      float vn[8], wn[8];  // the next chunk of x and w, loaded a chunk ahead
+      rs_load8<BF16>(base, 0, lane, vn);
+      rs_load8<BF16>(wbase, 0, lane, wn);
       for (uint32_t c = 0; c < nchunks; ++c) {
-        if (c * 256 + 8 * lane >= extent) continue;  // lanes past a short row's end
         float v[8], wv[8], o[8];
-        rs_load8<BF16>(base, c, lane, v);
-        rs_load8<BF16>(wbase, c, lane, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[i] = vn[i];
+          wv[i] = wn[i];
+        }
+        if (c + 1 < nchunks) {
+          rs_load8<BF16>(base, c + 1, lane, vn);
+          rs_load8<BF16>(wbase, c + 1, lane, wn);
+        }
+        if (c * 256 + 8 * lane >= extent) continue;  // lanes past a short row's end
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
           float t0, t1;

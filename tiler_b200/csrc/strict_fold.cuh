@@ -107,6 +107,33 @@ __device__ __forceinline__ void fold_after_add(NonnegFold& F, float s, float (&a
   fold_enter_fast(F, s);
 }
 
+// Two binary32 operations at once on the f32x2 ALU; each half is the IEEE RN
+// result of its own operands.
+__device__ __forceinline__ void fold_mul2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
+  uint64_t x, y, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(r));
+}
+__device__ __forceinline__ void fold_add2(float a0, float a1, float b0, float b1, float& r0, float& r1) {
+  uint64_t x, y, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(r));
+}
+// a * b + c with one rounding per half (used only where the result is exact)
+__device__ __forceinline__ void fold_fma2(float a0, float a1, float b0, float b1, float c0, float c1, float& r0,
+                                          float& r1) {
+  uint64_t x, y, z, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(z) : "f"(c0), "f"(c1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(y), "l"(z));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r0), "=f"(r1) : "l"(r));
+}
+
 __device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
   uint32_t r;
   asm volatile("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
@@ -125,17 +152,24 @@ __device__ __forceinline__ void fold_chunk(NonnegFold& F, float (&a)[8], uint32_
     if (F.mode == kFoldSmall) {
       // one term at a time, until the running value reaches 2^-103 (and at
       // least the first F.serial terms)
+      // (lane l's 8 terms are fetched at once and added in order; the running
+      // value is kept at the term where small mode ends)
       float s = F.s;
       int j = -1;
       for (int l = 0; l < 32 && j < 0; ++l) {
+        float t[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) t[k] = __shfl_sync(0xffffffffu, a[k], l);
+        float r = s;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const float t = __shfl_sync(0xffffffffu, a[k], l);
-          if (j < 0) {
-            s = __fadd_rn(s, t);
-            if (!(s < kFoldFastMin) && 8 * l + k + 1 >= F.serial) j = 8 * l + k;  // also taken for NaN
+          r = __fadd_rn(r, t[k]);
+          if (j < 0 && !(r < kFoldFastMin) && 8 * l + k + 1 >= F.serial) {  // also taken for NaN
+            j = 8 * l + k;
+            s = r;
           }
         }
+        if (j < 0) s = r;
       }
       F.serial = 0;
       if (j < 0) { F.s = s; return; }  // the whole chunk stayed small
@@ -146,24 +180,49 @@ __device__ __forceinline__ void fold_chunk(NonnegFold& F, float (&a)[8], uint32_
     // t = a * 2^(23-e) exactly; q = rint(t); a tie where |t - q| = 1/2, whose
     // integer part n = floor(t) is kept in v.  t is clamped to 2^23 first:
     // S >= 2^23, so any term that large crosses, and NaN / inf terms clamp to
-    // it too (min returns the non-NaN operand).
+    // it too (min returns the non-NaN operand).  rint is one add: t + 2^23
+    // lies in [2^23, 2^24], where the binary32 spacing is 1, so the add rounds
+    // t to the nearest integer, ties to even (2^23 is even), and that integer
+    // is the sum's bit pattern minus 2^23's (conversion instructions, which
+    // issue at a quarter of the rate, are avoided).
+    // Pairs of terms go through the f32x2 ALU (mul / add / fma .rn.f32x2,
+    // each half one IEEE RN operation).  The sum of q is taken from the bit
+    // patterns; the per-term values and tie bits are formed only where a tie
+    // or a crossing needs them.
+    float t[8], m[8], d[8];
+    uint32_t bsum = 0;
+    bool any_tie = false;
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      fold_mul2(a[k], a[k + 1], F.p, F.p, t[k], t[k + 1]);
+      t[k] = fminf(t[k], 8388608.0f);
+      t[k + 1] = fminf(t[k + 1], 8388608.0f);
+      fold_add2(t[k], t[k + 1], 8388608.0f, 8388608.0f, m[k], m[k + 1]);
+      float r0, r1;
+      fold_add2(m[k], m[k + 1], -8388608.0f, -8388608.0f, r0, r1);
+      fold_fma2(r0, r1, -1.0f, -1.0f, t[k], t[k + 1], d[k], d[k + 1]);  // t - r, exact
+      any_tie |= fabsf(d[k]) == 0.5f;
+      any_tie |= fabsf(d[k + 1]) == 0.5f;
+      bsum += __float_as_uint(m[k]) + __float_as_uint(m[k + 1]);
+    }
+    uint32_t vsum = bsum - 8u * 0x4b000000u;
     uint32_t v[8];
     uint32_t ties = 0;  // bit k: term k is a tie
-    uint32_t vsum = 0;
+    auto exact_terms = [&]() {
+      vsum = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float t = fminf(__fmul_rn(a[k], F.p), 8388608.0f);
-      const float q = rintf(t);
-      const float d = __fsub_rn(t, q);
-      const bool tie = fabsf(d) == 0.5f;
-      v[k] = (uint32_t)__float2int_rn(q) - (uint32_t)(tie && d < 0.0f);
-      ties |= (uint32_t)tie << k;
-      vsum += v[k];
-    }
-    const uint32_t tie_lanes = __ballot_sync(0xffffffffu, ties != 0);
+      for (int k = 0; k < 8; ++k) {
+        const bool tie = fabsf(d[k]) == 0.5f;
+        v[k] = (__float_as_uint(m[k]) - 0x4b000000u) - (uint32_t)(tie && d[k] < 0.0f);
+        ties |= (uint32_t)tie << k;
+        vsum += v[k];
+      }
+    };
+    const uint32_t tie_lanes = __ballot_sync(0xffffffffu, any_tie);
     uint32_t delta = 0;  // this lane's tie bits (0 without ties)
     uint32_t cin = 0;    // parity of the running value at this lane's first term
     if (tie_lanes) {
+      exact_terms();
       // lane-local parity walk: `par` = parity of the terms since the lane's
       // start or its last tie; x0 = that parity through the first tie
       uint32_t par = 0, x0 = 0, later = 0;
@@ -201,6 +260,7 @@ __device__ __forceinline__ void fold_chunk(NonnegFold& F, float (&a)[8], uint32_
       return;
     }
     // ---- a crossing: find its term (the running value is monotone) --------------
+    if (!tie_lanes) exact_terms();
     uint32_t c[8];  // each term's increment of S
     {
       uint32_t par = cin;

@@ -240,15 +240,19 @@ def softmax_masked(x: torch.Tensor, mask: torch.Tensor, row_offset: int = 0, out
     return y
 
 
-def rms_norm_quantize_i8(x: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, check=True):
+def rms_norm_quantize_i8(x: torch.Tensor, w: torch.Tensor, eps_bits: int = EPS_1E6_BITS, check=True, out=None):
     """Fused RMS norm -> per-row int8 quantize (f32): the codes and scales of
-    quantize_i8_rows(rms_norm(x, w)) without writing y."""
+    quantize_i8_rows(rms_norm(x, w)) without writing y.  ``out`` = (codes,
+    scales) to write into."""
     assert x.dtype == torch.float32 and w.dtype == torch.float32
     extent = x.shape[-1]
     rows = x.numel() // extent if extent else 0
     stride = 0 if w.dim() == 1 else extent
-    codes = torch.empty(x.shape, dtype=torch.int8, device=x.device)
-    scales = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    if out is None:
+        codes = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+        scales = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    else:
+        codes, scales = out
     st = _status() if check else None
     _check(N.lib().tiler_cuda_rms_norm_quantize_i8(context(), _stream(), st.ptr if st else 0, _ptr(x), _ptr(w), stride,
                                                    rows, extent, eps_bits, _ptr(codes), _ptr(scales)),
@@ -301,14 +305,18 @@ def softmax(x: torch.Tensor, causal_period: int = 0, row_offset: int = 0, out=No
     return y
 
 
-def quantize_i8_rows(x: torch.Tensor, check=True):
+def quantize_i8_rows(x: torch.Tensor, check=True, out=None):
     """Per-row signed strict-affine quantize (extension of quantization.rs:
-    188-247, :404-430).  Returns (codes int8, scales f32)."""
+    188-247, :404-430).  Returns (codes int8, scales f32), written into
+    ``out`` = (codes, scales) when given."""
     assert x.dtype == torch.float32
     extent = x.shape[-1]
     rows = x.numel() // extent
-    codes = torch.empty(x.shape, dtype=torch.int8, device=x.device)
-    scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+    if out is None:
+        codes = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+        scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+    else:
+        codes, scales = out
     st = _status() if check else None
     _check(N.lib().tiler_cuda_quantize_i8_rows(context(), _stream(), st.ptr if st else 0, _ptr(x), rows, extent,
                                                _ptr(codes), _ptr(scales)), "quantize_i8_rows")
