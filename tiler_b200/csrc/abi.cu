@@ -130,12 +130,14 @@ const Entry kEntries[] = {
     {"tiler_cuda.sum_f32.strict", (const void*)serial_folds_kernel<true>, kSerialFoldThreads, 0},
     {"tiler_cuda.sum_f32.partitioned", (const void*)serial_folds_kernel<false>, kSerialFoldThreads, 0},
     {"tiler_cuda.sum_f32.cooperative", (const void*)cooperative_sum_kernel, 1024, 0},
-    {"tiler_cuda.rms_norm_f32", (const void*)tiler_rms_norm_f32, kRsThreads, kRsSmemBytes, "tiler_rms_norm_f32"},
-    {"tiler_cuda.rms_norm_bf16", (const void*)tiler_rms_norm_bf16, kRsThreads, kRsSmemBytes, "tiler_rms_norm_bf16"},
+    {"tiler_cuda.rms_norm_f32", (const void*)tiler_rms_norm_wave_f32, kRmsThreads, kRmsSmemBytes,
+     "tiler_rms_norm_wave_f32"},
+    {"tiler_cuda.rms_norm_bf16", (const void*)tiler_rms_norm_wave_bf16, kRmsThreads, kRmsSmemBytes,
+     "tiler_rms_norm_wave_bf16"},
     {"tiler_cuda.softmax_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.quantize_i8_rows", (const void*)quantize_i8_rows_kernel, kQThreads, 0},
-    {"tiler_cuda.rms_norm_quantize_i8", (const void*)tiler_rms_norm_quantize_i8, kRsThreads, kRsSmemBytes,
-     "tiler_rms_norm_quantize_i8"},
+    {"tiler_cuda.rms_norm_quantize_i8", (const void*)tiler_rms_norm_wave_quantize_i8, kRmsThreads, kRmsSmemBytes,
+     "tiler_rms_norm_wave_quantize_i8"},
     {"tiler_cuda.softmax_masked_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.dequantize_i8_rows", (const void*)dequantize_i8_rows_kernel, 256, 0},
     {"tiler_cuda.quantize_affine_u8", (const void*)quantize_affine_u8_kernel, 256, 0},

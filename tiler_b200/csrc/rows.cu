@@ -10,6 +10,7 @@
 // one write per element.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "tmap.cuh"
 
 namespace tc {
@@ -233,10 +234,10 @@ __device__ __forceinline__ int code_of_bounded(float xv, float scale, float inv)
 // writing y, each normalize warp forms its row's y twice from the L2-resident
 // x (max|y| first, then the codes), so y never reaches HBM.
 template <bool BF16, bool QUANT = false>
-__global__ void __launch_bounds__(kRmsThreads, 1)
-    rms_norm_kernel(const uint8_t* __restrict__ x, const uint8_t* __restrict__ w, int64_t w_row_stride,
-                    uint64_t rows, uint64_t extent, float eps, uint8_t* __restrict__ y, uint32_t wave_rows,
-                    tiler_cuda_status* st, int8_t* __restrict__ codes = nullptr, float* __restrict__ scales = nullptr) {
+__device__ __forceinline__ void rms_norm_wave(const uint8_t* __restrict__ x, const uint8_t* __restrict__ w,
+                                              int64_t w_row_stride, uint64_t rows, uint64_t extent, float eps,
+                                              uint8_t* __restrict__ y, uint32_t wave_rows, tiler_cuda_status* st,
+                                              int8_t* __restrict__ codes, float* __restrict__ scales) {
   using E = RmsElem<BF16>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   RmsSmem& SS = *reinterpret_cast<RmsSmem*>(smem_raw);
@@ -469,6 +470,26 @@ __global__ void __launch_bounds__(kRmsThreads, 1)
   }
 }
 
+}  // namespace tc
+
+#define TILER_RMS_WAVE_PARAMS                                                                                  \
+  const uint8_t *__restrict__ x, const uint8_t *__restrict__ w, int64_t w_row_stride, uint64_t rows,          \
+      uint64_t extent, float eps, uint8_t *__restrict__ y, uint32_t wave_rows, tiler_cuda_status *st,          \
+      int8_t *__restrict__ codes, float *__restrict__ scales
+extern "C" __global__ void __launch_bounds__(tc::kRmsThreads, 1) tiler_rms_norm_wave_f32(TILER_RMS_WAVE_PARAMS) {
+  tc::rms_norm_wave<false, false>(x, w, w_row_stride, rows, extent, eps, y, wave_rows, st, codes, scales);
+}
+extern "C" __global__ void __launch_bounds__(tc::kRmsThreads, 1) tiler_rms_norm_wave_bf16(TILER_RMS_WAVE_PARAMS) {
+  tc::rms_norm_wave<true, false>(x, w, w_row_stride, rows, extent, eps, y, wave_rows, st, codes, scales);
+}
+extern "C" __global__ void __launch_bounds__(tc::kRmsThreads, 1)
+    tiler_rms_norm_wave_quantize_i8(TILER_RMS_WAVE_PARAMS) {
+  tc::rms_norm_wave<false, true>(x, w, w_row_stride, rows, extent, eps, y, wave_rows, st, codes, scales);
+}
+#undef TILER_RMS_WAVE_PARAMS
+
+namespace tc {
+
 // Any-shape path (unaligned rows or extents not a multiple of 16 bytes): one
 // warp per row, lane 0 folds the squares straight from global memory.
 template <bool BF16>
@@ -502,14 +523,17 @@ __global__ void rms_norm_generic_kernel(const void* __restrict__ xv, const void*
   }
 }
 
-// TILER_RMS_FORM=wave in the environment (read once per process) selects the
-// wave kernel above for every shape; it is how the two forms are compared.
-static bool rms_wave_form_forced() {
-  static const bool forced = [] {
+// TILER_RMS_FORM=scan in the environment (read once per process) selects the
+// warp-per-row kernel (rms_scan.cu) where it applies: exact as well, and
+// measured slower than the wave kernel at the BASELINE shapes (its per-row
+// fold is latency-bound with 12 rows in flight per SM), so the wave kernel is
+// the default.
+static bool rms_scan_form_selected() {
+  static const bool scan = [] {
     const char* v = getenv("TILER_RMS_FORM");
-    return v && strcmp(v, "wave") == 0;
+    return v && strcmp(v, "scan") == 0;
   }();
-  return forced;
+  return scan;
 }
 
 int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
@@ -519,14 +543,15 @@ int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_st
   const bool aligned = ((uintptr_t)x % 16 == 0) && ((uintptr_t)w % 16 == 0) && ((uintptr_t)codes % 4 == 0) &&
                        extent % 4 == 0;
   if (!aligned) return TILER_CUDA_UNSUPPORTED;
-  if (!rms_wave_form_forced() &&
+  if (rms_scan_form_selected() &&
       rms_scan_launch(0, 1, x, w, w_row_stride, rows, extent, eps, nullptr, codes, scales, st, sm_count, stream))
     return 0;
   const uint64_t grid = umin64((uint64_t)sm_count, rows);
-  cudaFuncSetAttribute(rms_norm_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
-  rms_norm_kernel<false, true><<<(unsigned)grid, kRmsThreads, kRmsSmemBytes, stream>>>(
-      (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, nullptr, (uint32_t)kRmsWave, st, codes,
-      scales);
+  cudaFuncSetAttribute(tiler_rms_norm_wave_quantize_i8, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)kRmsSmemBytes);
+  launch_kernel((const void*)tiler_rms_norm_wave_quantize_i8, "tiler_rms_norm_wave_quantize_i8", dim3((unsigned)grid),
+                dim3(kRmsThreads), kRmsSmemBytes, stream, (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows,
+                extent, eps, (uint8_t*)nullptr, (uint32_t)kRmsWave, st, codes, scales);
   return 0;
 }
 
@@ -545,22 +570,18 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
       rms_norm_generic_kernel<false><<<blocks, wpb * 32, 0, stream>>>(x, w, w_row_stride, rows, extent, eps, y);
     return 0;
   }
-  // The warp-per-row form where it applies (broadcast weights, rows up to 16 KB)
-  if (!rms_wave_form_forced() &&
+  // The warp-per-row form when selected and where it applies (broadcast
+  // weights, rows up to 16 KB)
+  if (rms_scan_form_selected() &&
       rms_scan_launch(bf16, 0, x, w, w_row_stride, rows, extent, eps, y, nullptr, nullptr, st, sm_count, stream))
     return 0;
-  // Otherwise one CTA per SM; each takes rows/grid consecutive rows in waves.
+  // One CTA per SM; each takes rows/grid consecutive rows in waves.
   const uint64_t grid = umin64((uint64_t)sm_count, rows);
-  const uint32_t wave = (uint32_t)kRmsWave;
-  if (bf16) {
-    cudaFuncSetAttribute(rms_norm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
-    rms_norm_kernel<true><<<(unsigned)grid, kRmsThreads, kRmsSmemBytes, stream>>>(
-        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, wave, st);
-  } else {
-    cudaFuncSetAttribute(rms_norm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
-    rms_norm_kernel<false><<<(unsigned)grid, kRmsThreads, kRmsSmemBytes, stream>>>(
-        (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows, extent, eps, (uint8_t*)y, wave, st);
-  }
+  const void* fn = bf16 ? (const void*)tiler_rms_norm_wave_bf16 : (const void*)tiler_rms_norm_wave_f32;
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRmsSmemBytes);
+  launch_kernel(fn, bf16 ? "tiler_rms_norm_wave_bf16" : "tiler_rms_norm_wave_f32", dim3((unsigned)grid),
+                dim3(kRmsThreads), kRmsSmemBytes, stream, (const uint8_t*)x, (const uint8_t*)w, w_row_stride, rows,
+                extent, eps, (uint8_t*)y, (uint32_t)kRmsWave, st, (int8_t*)nullptr, (float*)nullptr);
   return 0;
 }
 
