@@ -426,6 +426,21 @@ def family_suite(fam, torch, world, steps_small, warmup):
                 rec("gemm_bf16_silu_nsharded_fused_allgather", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps,
                     tflops * world)
                 blocks.close()
+            # the all-gather as multicast stores into an NVLink multicast mapping (each box
+            # crosses NVLink once); available where torch symmetric memory offers one
+            try:
+                mblocks = sharding.MulticastBlocks((world, 8192, c1 - c0), torch.bfloat16, dev)
+            except Exception as exc:  # noqa: BLE001
+                mblocks = None
+                out["gemm_bf16_silu_nsharded_multicast_allgather"] = {"unavailable": str(exc)[:200]}
+            if mblocks is not None and not mblocks.available:
+                out["gemm_bf16_silu_nsharded_multicast_allgather"] = {"unavailable": "no multicast mapping"}
+            elif mblocks is not None:
+                ms = time_device(lambda i: sharding.gemm_n_sharded_multicast(
+                    ga, ws_, mblocks, lambda a_, w_, lp, mp, r_, n_: fam.gemm_bf16_allgather_multicast(
+                        a_, w_, lp, mp, r_, n_, "silu", check=False)), gsteps, warmup, world)
+                rec("gemm_bf16_silu_nsharded_multicast_allgather", "TFLOP/s", 2.0 * 8192 * 4096 * 14336, ms, gsteps,
+                    tflops * world)
     del table, ga, gas, wt, cc
     torch.cuda.empty_cache()
     out.update(strong_scaled_suite(fam, torch, world, steps_small, warmup))

@@ -359,6 +359,16 @@ int32_t tiler_cuda_gemm_bf16_allgather(tiler_cuda_context* ctx, void* stream, ti
                                        const uint16_t* a, const uint16_t* b_shard, uint64_t m, uint64_t n_shard,
                                        uint64_t k, int32_t epilogue, uint32_t rank, uint32_t world,
                                        void* const* blocks);
+/* The same exchange through an NVLink multicast mapping of every rank's
+ * [world, m, n_shard] buffer (NVSwitch replicates each store to every bound
+ * GPU): `local_buffer` is this rank's buffer, `multicast_buffer` the multicast
+ * address of the same buffer (e.g. torch symmetric memory's multicast_ptr).
+ * Each output box crosses NVLink once instead of once per peer.  The same two
+ * ordering collectives as above apply. */
+int32_t tiler_cuda_gemm_bf16_allgather_multicast(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                                 const uint16_t* a, const uint16_t* b_shard, uint64_t m,
+                                                 uint64_t n_shard, uint64_t k, int32_t epilogue, uint32_t rank,
+                                                 uint32_t world, void* local_buffer, void* multicast_buffer);
 
 #ifdef __cplusplus
 }

@@ -57,6 +57,25 @@ def _checks(rank, world):
     blocks.close()
     results["gemm_fused_allgather"] = bool(ok)
 
+    # the same exchange through an NVLink multicast mapping, where the box has one
+    try:
+        mblocks = sharding.MulticastBlocks((world, m, c1 - c0), torch.bfloat16, "cuda")
+        multicast = mblocks.available
+    except Exception:  # noqa: BLE001 - no symmetric memory on this box
+        multicast = False
+    results["multicast_available"] = multicast
+    if multicast:
+        ok = True
+        for call in range(2):
+            a = (torch.randn(m, k, device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+            want = sharding.gemm_n_sharded(a, ws, lambda aa, ww: fam.gemm_bf16(aa, ww, "silu"), assemble=False)
+            got = sharding.gemm_n_sharded_multicast(
+                a, ws, mblocks,
+                lambda aa, ww, lp, mp, r, nw: fam.gemm_bf16_allgather_multicast(aa, ww, lp, mp, r, nw, "silu"))
+            ok = ok and torch.equal(got.view(torch.int16), want.view(torch.int16))
+        torch.distributed.barrier()
+        results["gemm_multicast_allgather"] = bool(ok)
+
     # row-sharded RMS norm [8192, 4096] f32
     x = torch.randn(8192, 4096, device="cuda", generator=gen)
     wr = torch.rand(4096, device="cuda", generator=gen) + 0.5
@@ -122,4 +141,11 @@ def test_sharded_families_match_one_gpu(world):
         p.join(timeout=120)
     want = {"gemm_fused_allgather": True, "rms_row_shard": True, "softmax_row_shard": True,
             "sum_rank_ordered": True}
-    assert results == [(r, want) for r in range(world)], results
+    for r, res in results:
+        assert isinstance(res, dict), (r, res)
+        if res.pop("multicast_available"):
+            want_r = dict(want, gemm_multicast_allgather=True)
+        else:
+            want_r = want
+        assert res == want_r, (r, res)
+    assert [r for r, _ in results] == list(range(world))

@@ -108,6 +108,7 @@ SIGNATURES = {
     "tiler_cuda_ipc_open": (i32, [P, P, u64, P]),
     "tiler_cuda_ipc_close": (i32, [P, P, u64]),
     "tiler_cuda_gemm_bf16_allgather": (i32, [P, P, P, P, P, u64, u64, u64, i32, u32, u32, P]),
+    "tiler_cuda_gemm_bf16_allgather_multicast": (i32, [P, P, P, P, P, u64, u64, u64, i32, u32, u32, P, P]),
     "tiler_cuda_softmax_f32": (i32, [P, P, P, P, u64, u64, u64, u64, P]),
     "tiler_cuda_quantize_i8_rows": (i32, [P, P, P, P, u64, u64, P, P]),
     "tiler_cuda_dequantize_i8_rows": (i32, [P, P, P, P, P, u64, u64, P]),

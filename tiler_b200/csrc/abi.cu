@@ -849,4 +849,24 @@ int32_t tiler_cuda_gemm_bf16_allgather(tiler_cuda_context* ctx, void* stream, ti
   return last_error_status();
 }
 
+int32_t tiler_cuda_gemm_bf16_allgather_multicast(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* st,
+                                                 const uint16_t* a, const uint16_t* b_shard, uint64_t m,
+                                                 uint64_t n_shard, uint64_t k, int32_t epilogue, uint32_t rank,
+                                                 uint32_t world, void* local_buffer, void* multicast_buffer) {
+  CHECK_CTX(ctx);
+  if (epilogue != 0 && epilogue != 1) return TILER_CUDA_INVALID_APPLICATION;
+  if (k == 0 || world == 0 || rank >= world || !local_buffer || !multicast_buffer)
+    return TILER_CUDA_INVALID_APPLICATION;
+  if (m == 0 || n_shard == 0) return TILER_CUDA_OK;
+  if (!a || !b_shard) return TILER_CUDA_INVALID_APPLICATION;
+  if (m / 128 * (n_shard / 256) > 0xffffffffull || k > (1ull << 31)) return TILER_CUDA_SHAPE_TOO_LARGE;
+  const uint64_t block_elems = m * n_shard;
+  uint16_t* local = (uint16_t*)local_buffer + (uint64_t)rank * block_elems;
+  uint16_t* mc = (uint16_t*)multicast_buffer + (uint64_t)rank * block_elems;
+  int32_t r = launch_gemm_bf16(a, b_shard, m, n_shard, k, epilogue, local, n_shard, st, ctx->facts.sm_count,
+                               S(stream), nullptr, 0, mc);
+  if (r != TILER_CUDA_OK) return r;
+  return last_error_status();
+}
+
 }  // extern "C"

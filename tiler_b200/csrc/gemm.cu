@@ -79,6 +79,11 @@ constexpr int kGemmMaxPeers = 8;
 struct GemmPeers {
   uint16_t* block[kGemmMaxPeers];  // this rank's block inside each rank's buffer (nullptr: skip)
   uint32_t count;
+  // Or: this rank's block inside an NVLink multicast mapping of every rank's
+  // buffer.  One multimem.st per 16 bytes then reaches every rank's copy
+  // (this rank's included) through the switch, so each box crosses NVLink
+  // once instead of once per peer, and the local TMA store is skipped.
+  uint16_t* multicast;
 };
 
 // Epilogue staging: per epilogue warp one 32-row x 64-column bf16 box
@@ -193,14 +198,28 @@ __device__ __forceinline__ void gemm_epilogue_tile(uint32_t tmem_tile, uint32_t 
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
-    if (lane == 0) {
+    if (lane == 0 && !peers.multicast) {
       const int32_t x = (int32_t)(col_base + box), y = (int32_t)row_base;
       asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap_c),
                    "r"(x), "r"(y), "r"(stage_u32)
                    : "memory");
       asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
-    if (peers.count) {
+    if (peers.multicast) {
+      // the box to every rank at once: 8 lanes per 128-byte row, 4 rows per step
+      const uint32_t c = lane & 7, rr = lane >> 3;
+      const uint64_t col = col_base + box + c * 8;
+#pragma unroll
+      for (uint32_t r0 = 0; r0 < 32; r0 += 4) {
+        const uint32_t r = r0 + rr;
+        const uint4 v = lds_u4(stage_u32 + r * 128 + ((c ^ (r & 7)) * 16));
+        uint16_t* dst = peers.multicast + (row_base + r) * ldp + col;
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(v.x), "r"(v.y),
+                     "r"(v.z), "r"(v.w)
+                     : "memory");
+      }
+      __syncwarp();  // the staging buffer is rewritten by the next box
+    } else if (peers.count) {
       // the box to each peer: 8 lanes per 128-byte row, 4 rows per step
       const uint32_t c = lane & 7, rr = lane >> 3;
       const uint64_t col = col_base + box + c * 8;
@@ -310,7 +329,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     // the stores have completed before the CTA (and its shared memory) goes away
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    if (peers.count) __threadfence_system();  // the peer stores are visible before the kernel ends
+    if (peers.count || peers.multicast) __threadfence_system();  // the peer stores are visible before the kernel ends
   }
   tmem_fence_before();
   __syncthreads();
@@ -495,7 +514,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&B.tmem_empty[buf]), 0));
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-    if (peers.count) __threadfence_system();
+    if (peers.count || peers.multicast) __threadfence_system();
   }
   tmem_fence_before();
   cluster_sync_all();  // no arrival or load of one CTA targets the other after this
@@ -514,10 +533,12 @@ static bool make_tmap(CUtensorMap* map, const void* base, uint64_t rows, uint64_
 
 int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k, int epilogue,
                      uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream,
-                     uint16_t* const* peer_blocks, uint32_t npeers) {
+                     uint16_t* const* peer_blocks, uint32_t npeers, uint16_t* multicast) {
   if (npeers > (uint32_t)kGemmMaxPeers) return TILER_CUDA_UNSUPPORTED;
   GemmPeers peers{};
   peers.count = npeers;
+  peers.multicast = multicast;
+  if ((uintptr_t)multicast % 16) return TILER_CUDA_UNSUPPORTED;
   for (uint32_t q = 0; q < npeers; ++q) {
     peers.block[q] = peer_blocks[q];
     if (peer_blocks[q] && (uintptr_t)peer_blocks[q] % 16) return TILER_CUDA_UNSUPPORTED;

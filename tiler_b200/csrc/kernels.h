@@ -72,7 +72,7 @@ void launch_contract_f32(const float* a, const float* b, uint64_t m, uint64_t n,
 // rank (row pitch ldc); the all-gather fused into the epilogue.
 int launch_gemm_bf16(const uint16_t* a, const uint16_t* b, uint64_t m, uint64_t n, uint64_t k, int epilogue,
                      uint16_t* c, uint64_t ldc, tiler_cuda_status* st, int sm_count, cudaStream_t stream,
-                     uint16_t* const* peer_blocks = nullptr, uint32_t npeers = 0);
+                     uint16_t* const* peer_blocks = nullptr, uint32_t npeers = 0, uint16_t* multicast = nullptr);
 
 // Kernel registry (entry symbols for payload validation / entry queries).
 struct EntryInfo {

@@ -457,6 +457,25 @@ def gemm_bf16_allgather(a: torch.Tensor, b_shard: torch.Tensor, blocks, rank: in
         _raise_from(st, "gemm_bf16_allgather")
 
 
+def gemm_bf16_allgather_multicast(a: torch.Tensor, b_shard: torch.Tensor, local_buffer: int, multicast_buffer: int,
+                                  rank: int, world: int, epilogue: str = "silu", check=True):
+    """The fused N-sharded contraction with the all-gather done by multicast
+    stores (multimem.st) into an NVLink multicast mapping of every rank's
+    [world, m, n_shard] buffer: ``local_buffer`` is this rank's buffer and
+    ``multicast_buffer`` its multicast address."""
+    assert a.dtype == torch.bfloat16 and b_shard.dtype == torch.bfloat16
+    m, k = a.shape
+    n = b_shard.shape[0]
+    st = _status() if check else None
+    _check(N.lib().tiler_cuda_gemm_bf16_allgather_multicast(context(), _stream(), st.ptr if st else 0, a.data_ptr(),
+                                                            b_shard.data_ptr(), m, n, k,
+                                                            1 if epilogue == "silu" else 0, rank, world,
+                                                            local_buffer, multicast_buffer),
+           "gemm_bf16_allgather_multicast")
+    if st:
+        _raise_from(st, "gemm_bf16_allgather_multicast")
+
+
 def gemm_bf16(a: torch.Tensor, b: torch.Tensor, epilogue: str = "silu", out=None, check=True) -> torch.Tensor:
     """bf16 A[m,k] x B[n,k] on tcgen05 tensor cores, f32 accumulation,
     optional SiLU epilogue, bf16 output [m,n]."""

@@ -105,6 +105,46 @@ class PeerBlocks:
         self._opened = []
 
 
+class MulticastBlocks:
+    """A [world, m, n] block buffer in torch symmetric memory on every rank,
+    with its NVLink multicast address when the GPUs and driver offer one
+    (``available``).  The fused GEMM's multicast stores into it reach every
+    rank's copy at once."""
+
+    def __init__(self, shape, dtype, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        assert shape[0] == self.world
+        group = group or dist.group.WORLD
+        name = group.group_name
+        if hasattr(symm_mem, "enable_symm_mem_for_group"):
+            try:
+                symm_mem.enable_symm_mem_for_group(name)
+            except Exception:  # noqa: BLE001 - newer releases enable it themselves
+                pass
+        self.local = symm_mem.empty(shape, dtype=dtype, device=device)
+        self.handle = symm_mem.rendezvous(self.local, name)
+        base = int(self.handle.multicast_ptr or 0)
+        self.available = base != 0
+        self.local_ptr = self.local.data_ptr()
+        offset = self.local_ptr - int(self.handle.buffer_ptrs[self.handle.rank])
+        self.multicast_ptr = base + offset if self.available else 0
+
+
+def gemm_n_sharded_multicast(a: torch.Tensor, w_shard: torch.Tensor, blocks: MulticastBlocks, fused_gemm, group=None):
+    """``gemm_n_sharded_fused`` over multicast: ``fused_gemm(a, w_shard,
+    local_ptr, multicast_ptr, rank, world)`` stores this rank's columns once,
+    and the switch delivers them to every rank.  The same two one-element
+    all-reduces order the call (before: every rank has finished reading the
+    previous result; after: every rank's stores have landed)."""
+    ready = torch.zeros(1, device=a.device)
+    dist.all_reduce(ready, group=group)
+    fused_gemm(a, w_shard, blocks.local_ptr, blocks.multicast_ptr, blocks.rank, blocks.world)
+    done = torch.zeros(1, device=a.device)
+    dist.all_reduce(done, group=group)
+    return blocks.local
+
+
 def gemm_n_sharded_fused(a: torch.Tensor, w_shard: torch.Tensor, blocks: PeerBlocks, fused_gemm, group=None):
     """The contraction's multi-GPU form with the exchange fused into the GEMM:
     ``fused_gemm(a, w_shard, ptrs, rank, world)`` writes this rank's columns
