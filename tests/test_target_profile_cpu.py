@@ -66,3 +66,37 @@ def test_work_span_fit_recovers_a_known_model():
     (key, value, scope), = prof["cost"]
     assert key == "cost.saturated-parallel-fold-steps" and scope == "MeasuredEnvironment" and value > 0
     assert tp.target_profile()["cost"] == []  # silence without a measurement
+
+
+def test_committed_rust_declarations_are_the_rendering_of_these_rows():
+    """tiler_b200/rust/tiler_cuda_profile.rs is what the crate compiles: it
+    must be the current rendering, one builder call per row."""
+    text = tp.render_rust(measured_fold_steps=tp.MEASURED_FOLD_STEPS)
+    assert open(tp.RUST_PATH).read() == text, "regenerate with python -m tiler_b200.target_profile --rust"
+    prof = tp.target_profile(measured_fold_steps=tp.MEASURED_FOLD_STEPS)
+    calls = re.findall(r"builder\.(declare_\w+)\(", text)
+    want = len(prof["capability"]) + len(prof["numerics"]) + len(prof["dtype_dispatchability"]) + \
+        len(prof["subgroup_realization"]) + len(prof["cost"])
+    assert len(calls) == want
+    # every declaration is one of TargetProfileBuilder's own methods
+    # (crates/tiler-compiler/src/target/builder.rs:97-1439)
+    builder_methods = {
+        "declare_max_threads_per_grid_axis", "declare_max_threads_per_workgroup",
+        "declare_max_buffer_bindings_per_entry", "declare_index_arithmetic", "declare_device_address_width",
+        "declare_device_memory", "declare_local_memory_bytes", "declare_input_subnormals",
+        "declare_result_subnormals", "declare_contraction", "declare_reassociation", "declare_permutation",
+        "declare_signed_zero", "declare_reciprocal_transform", "declare_approximate_intrinsics",
+        "declare_nan_assumptions", "declare_infinity_assumptions", "declare_dtype_dispatchability",
+        "declare_subgroup_realization", "declare_measured_saturated_parallel_fold_steps"}
+    assert set(calls) <= builder_methods
+    caps = dict(prof["capability"])
+    assert f"declare_local_memory_bytes({caps['local_memory_bytes']}," in text
+    assert f"declare_measured_saturated_parallel_fold_steps({tp.MEASURED_FOLD_STEPS}, source)" in text
+    # braces and parentheses balance
+    assert text.count("{") == text.count("}") and text.count("(") == text.count(")")
+    # the payload metadata names exactly the entries the cubin carries, and the build flags
+    syms = re.findall(r'symbol: "([^"]+)"', text)
+    assert sorted(syms) == sorted(tp.MODULE_ENTRY_SYMBOLS)
+    registry = {e["symbol"] for e in tp.payload_entries()}
+    assert set(syms) <= registry
+    assert '"-fmad=false".to_owned()' in text and '"sm_100a".to_owned()' in text

@@ -234,8 +234,8 @@ def _nvcc_version() -> str:
 
 
 def payload_provenance() -> dict:
-    """PayloadMetadata provenance fields (payload.rs:228-424) for
-    libtiler_cuda.so."""
+    """PayloadMetadata provenance fields (payload.rs:228-424) for the sm_100a
+    code (tiler_kernels.cubin, launched by libtiler_cuda.so)."""
     compile_flags, link_flags = _makefile_flags()
     return {
         "toolchain": _nvcc_version(),
@@ -243,7 +243,10 @@ def payload_provenance() -> dict:
         "family": "tiler-cuda",
         "language": "cuda-c++17",
         "platform": "Unversioned",
-        "components": ["libtiler_cuda.so"],
+        # the tools that produced the code (ToolComponent {role, version})
+        "components": [{"role": "cuda-compiler", "version": _nvcc_version().replace("nvcc ", "")}],
+        # what the payload carries: the code bytes and the host library that launches them
+        "artifacts": ["tiler_kernels.cubin", "libtiler_cuda.so"],
         "compile_flags": compile_flags,
         "link_flags": link_flags,
     }
@@ -259,8 +262,15 @@ def payload_entries() -> list:
     return out
 
 
-if __name__ == "__main__":
-    # python -m tiler_b200.target_profile: the dispatch sweep and its fit on cuda:0
+def _main():
+    import sys
+    if "--rust" in sys.argv:
+        os.makedirs(os.path.dirname(RUST_PATH), exist_ok=True)
+        with open(RUST_PATH, "w") as f:
+            f.write(render_rust(measured_fold_steps=MEASURED_FOLD_STEPS))
+        print(RUST_PATH)
+        return
+    # the dispatch sweep and its fit on cuda:0
     import json
 
     import torch
@@ -273,3 +283,164 @@ if __name__ == "__main__":
                       "cost": cost_rows(round(fit["parallel_steps"])),
                       "cells": [{k: v for k, v in c.items() if k != "stages"} | {"stages": c["stages"]}
                                 for c in cells]}))
+
+
+# ---- Rust source for the tiler-cuda crate ---------------------------------------
+#
+# The rows above rendered as the crate's own declaration code: one
+# TargetProfileBuilder call per row (method names and argument types as in
+# crates/tiler-compiler/src/target/builder.rs:97-1439, sources as in the
+# custom-backend precedent crates/tiler-build/tests/custom_backend/
+# profile.rs:102-253 and the measured cost row as in crates/tiler-build/src/
+# metal_declaration.rs:1012-1016), and the PayloadMetadata the artifact carries
+# for the sm_100a cubin (crates/tiler-artifact/src/program/codec/payload.rs:
+# 228-424).  ``tiler_b200/rust/tiler_cuda_profile.rs`` is this rendering,
+# regenerated by ``python -m tiler_b200.target_profile --rust``; a CPU test
+# keeps the committed file equal to it.
+
+_SUBNORMAL_RUST = {
+    "Preserve": "SubnormalMode::Preserve",
+    "FlushToZero{PreservesSign}": "SubnormalMode::FlushToZero { zero_sign: FlushedZeroSign::PreservesSign }",
+    "FlushToZero{AlwaysPositive}": "SubnormalMode::FlushToZero { zero_sign: FlushedZeroSign::AlwaysPositive }",
+}
+_PERMISSION_AXES = ("contraction", "reassociation", "permutation", "signed_zero", "reciprocal_transform")
+_RUST_DTYPES = {"f32": "F32::resolved_type()", "bf16": "Bf16::resolved_type()"}
+
+
+def _rust_str(s: str) -> str:
+    return '"' + s.replace("\\", "\\\\").replace('"', '\\"') + '"'
+
+
+def render_rust(facts: dict | None = None, measured_fold_steps: int | None = None, provenance: dict | None = None,
+                entries: list | None = None) -> str:
+    """The crate's profile and payload declarations as Rust source text."""
+    prof = target_profile(facts, measured_fold_steps)
+    prov = provenance if provenance is not None else payload_provenance()
+    if entries is None:  # the entries whose kernels the code payload carries
+        entries = [e for e in payload_entries() if e["symbol"] in MODULE_ENTRY_SYMBOLS]
+    ents = entries
+    L = []
+    w = L.append
+    w("// The tiler-cuda crate's target profile and payload metadata.")
+    w("// Generated from tiler_b200/target_profile.py by")
+    w("// `python -m tiler_b200.target_profile --rust`; regenerate, do not edit.")
+    w("")
+    w(f"pub const PROFILE_KEY: &str = {_rust_str(prof['key'])};")
+    producer, revision = prof["source"]["producer"]
+    w(f"pub const PRODUCER: &str = {_rust_str(producer)};")
+    w("")
+    w("fn guarantee(reference: &str) -> Result<TargetFactSource, TargetProfileBuildError> {")
+    w(f"    let producer = TargetFactProducerIdentity::new(PRODUCER.to_owned(), {revision})")
+    w("        .map_err(|_| TargetProfileBuildError::InvalidProducerClaim)?;")
+    w("    let reference = TargetNormativeReferenceIdentity::new(reference.to_owned(), 1)")
+    w("        .map_err(|_| TargetProfileBuildError::InvalidProducerClaim)?;")
+    w("    Ok(TargetFactSource::external_guarantee(producer, reference))")
+    w("}")
+    w("")
+    w("/// The sm_100a profile.  `cost_source` carries the measurement context of")
+    w("/// the fold-step sweep (nvcc build, the B200 execution environment).")
+    w("pub fn cuda_sm100a_profile(")
+    w("    cost_source: Option<TargetCompileProfileMeasurementSource>,")
+    w(") -> Result<TargetProfile, TargetProfileBuildError> {")
+    w("    let key = TargetProfileKey::new(PROFILE_KEY.to_owned())")
+    w("        .map_err(|_| TargetProfileBuildError::InvalidProducerClaim)?;")
+    w("    let mut builder = TargetProfileBuilder::new(key);")
+    ieee, ptx = prof["source"]["references"]
+    w(f"    let ieee = guarantee({_rust_str(ieee)})?;")
+    w(f"    let ptx = guarantee({_rust_str(ptx)})?;")
+    w("")
+    w("    // capability rows (tiler_cuda_device_facts_query)")
+    for name, value in prof["capability"]:
+        if name == "index_arithmetic":
+            arg = f"IndexArithmeticSupport::{value}"
+        elif name == "device_address_width":
+            arg = f"DeviceAddressWidth::{value}"
+        elif name == "device_memory":
+            arg = "true" if value else "false"
+        else:
+            arg = str(int(value))
+        w(f"    builder.declare_{name}({arg}, ptx.clone())?;")
+    w("")
+    w("    // numerics rows: what every kernel does (IEEE binary32, one rounding per operator)")
+    w("    let f32_subject = ScalarArithmetic::f32();")
+    for subject, axis, behaviour, support in prof["numerics"]:
+        if axis in ("input_subnormals", "result_subnormals"):
+            arg = _SUBNORMAL_RUST[behaviour]
+        elif axis in _PERMISSION_AXES:
+            arg = "NumericalPermission::Permitted" if behaviour.startswith("Permitted") else \
+                "NumericalPermission::Forbidden"
+        elif axis == "approximate_intrinsics":
+            arg = f"ApproximationEnvelope::{behaviour}"
+        else:
+            arg = f"ExceptionalValueAssumption::{behaviour}"
+        if behaviour == "Permitted(declared grouping)":
+            w("    // permitted only as the grouping a provider proposal declares (the grid grouping)")
+        w(f"    builder.declare_{axis}(f32_subject.clone(), {arg}, ScalarSupport::{support}, ieee.clone())?;")
+    w("")
+    w("    // dtype dispatchability")
+    for dtype, verdict in prof["dtype_dispatchability"]:
+        w(f"    builder.declare_dtype_dispatchability({_RUST_DTYPES[dtype]}, DTypeDispatchability::{verdict}, "
+          "ptx.clone())?;")
+    w("")
+    w("    // the subgroup realization of the grouped fold's butterfly")
+    for subj, verdict in prof["subgroup_realization"]:
+        w("    let subject = SubgroupRealizationSubject::new(")
+        w(f"        SubgroupWidth::new({subj['width']}).map_err(|_| TargetProfileBuildError::InvalidProducerClaim)?,")
+        w(f"        ArithmeticType::{subj['element']},")
+        w("        SubgroupTransfer::InRangeXorShuffle,")
+        w("    )")
+        w("    .map_err(|_| TargetProfileBuildError::InvalidProducerClaim)?;")
+        support = "Realized" if verdict == "Supported" else "Unrealizable"
+        w(f"    builder.declare_subgroup_realization(subject, SubgroupSupport::{support}, ptx.clone())?;")
+    w("")
+    w("    // the measured cost row (a dispatch sweep on one B200; silence states no preference)")
+    rows = prof["cost"]
+    if rows:
+        _, steps, _ = rows[0]
+        w("    if let Some(source) = cost_source {")
+        w(f"        builder.declare_measured_saturated_parallel_fold_steps({int(steps)}, source)?;")
+        w("    }")
+    else:
+        w("    let _ = cost_source;")
+    w("    builder.build()")
+    w("}")
+    w("")
+    w("/// PayloadMetadata for the sm_100a cubin (`code` = tiler_kernels.cubin).")
+    w("pub fn cuda_payload_metadata(source_representation: RepresentationKey) -> PayloadMetadata {")
+    w("    PayloadMetadata {")
+    w("        source_representation,")
+    w("        source: Vec::new(),")
+    w("        provenance: PayloadProvenance {")
+    for field in ("toolchain", "target", "family", "language"):
+        w(f"            {field}: {_rust_str(prov[field])}.to_owned(),")
+    w("            platform: PayloadPlatform::Unversioned,")
+    w("            components: vec![")
+    for comp in prov["components"]:
+        w(f"                ToolComponent {{ role: {_rust_str(comp['role'])}.to_owned(), "
+          f"version: {_rust_str(comp['version'])}.to_owned() }},")
+    w("            ],")
+    w("            compile_flags: vec![" + ", ".join(f"{_rust_str(f)}.to_owned()" for f in prov["compile_flags"]) + "],")
+    w("            link_flags: vec![" + ", ".join(f"{_rust_str(f)}.to_owned()" for f in prov["link_flags"]) + "],")
+    w("        },")
+    w("        entries: vec![")
+    for e in ents:
+        w(f"            PayloadEntryMapping {{ entry_key: BackendEntryKey::new({_rust_str(e['entry_key'])}.to_owned())"
+          f".expect(\"entry key\"), symbol: {_rust_str(e['symbol'])}.to_owned(), transports: Vec::new() }},")
+    w("        ],")
+    w("        obligations: vec![PayloadTargetObligation { key: \"subgroup-width\".to_owned(), value: \"32\".to_owned() }],")
+    w("    }")
+    w("}")
+    return "\n".join(L) + "\n"
+
+
+# Entries whose kernels tiler_kernels.cubin carries (tiler_cuda_module_entry
+# accepts exactly these; csrc/launch.cuh lists the kernels).
+MODULE_ENTRY_SYMBOLS = ("tiler_cuda.sum_f32.grouped", "tiler_cuda.max_f32.grouped", "tiler_cuda.rms_norm_f32",
+                        "tiler_cuda.rms_norm_bf16", "tiler_cuda.rms_norm_quantize_i8")
+RUST_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "rust", "tiler_cuda_profile.rs")
+# the fold-step row as measured on one B200 (python -m tiler_b200.target_profile)
+MEASURED_FOLD_STEPS = 10571
+
+
+if __name__ == "__main__":
+    _main()
