@@ -513,7 +513,27 @@ def strong_scaled_suite(fam, torch, world, steps_small, warmup):
             L.tiler_cuda_strict_sum_f32(ctx, cur_stream(), gathered.data_ptr(), 1, world, total.data_ptr())
     steps = steps_small * 8
     ms = time_device(run_sum, steps, warmup, world)
-    rec("strong_sum_f32_2^24_rank_ordered", n * 4, ms, steps, f"{s1 - s0} contributors per rank")
+    rec("strong_sum_f32_2^24_rank_ordered_nccl", n * 4, ms, steps, f"{s1 - s0} contributors per rank")
+    # the exchange as one kernel: partials stored over NVLink into every rank's
+    # buffer, each rank folding the W partials in rank order
+    xch = None
+    if world > 1:
+        try:
+            xch = sharding.SumExchange(1, dev, fam.ipc_export, fam.ipc_open, fam.ipc_close)
+        except RuntimeError as exc:
+            out["strong_sum_f32_2^24_rank_ordered"] = {"unavailable": str(exc)[:200]}
+
+    def run_sum_xch(i):
+        L.tiler_cuda_sum_f32(ctx, cur_stream(), shards[i % 4].data_ptr(), 1, s1 - s0, C.byref(gs), ws.data_ptr(),
+                             ws.numel(), part.data_ptr())
+        if xch is not None:
+            xch(part, out=total, check=False)
+    if world == 1 or xch is not None:
+        ms = time_device(run_sum_xch, steps, warmup, world)
+        rec("strong_sum_f32_2^24_rank_ordered", n * 4, ms, steps, f"{s1 - s0} contributors per rank")
+    if xch is not None:
+        torch.distributed.barrier()
+        xch.close()
     del shards
     return out
 

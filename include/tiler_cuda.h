@@ -210,6 +210,20 @@ int32_t tiler_cuda_max_f32(tiler_cuda_context* ctx, void* stream, const float* x
  * overlap on the GPU share the array and race.  Allocates nothing. */
 int32_t tiler_cuda_sum_f32_no_alloc(tiler_cuda_context* ctx, void* stream, const float* x, uint64_t rows,
                                     uint64_t count, const tiler_cuda_grouping* g, float* out);
+/* The multi-GPU sum's exchange (the declared order: partition r = rank r's
+ * shard, folded strictly in rank order as strict_partitioned_sum does,
+ * evaluate.rs:749-832): `partial` [rows] is this rank's shard sum (e.g. from
+ * tiler_cuda_sum_f32); it is stored over NVLink into slot `rank` of every
+ * rank's exchange buffer (`buffers[q]`: rank q's buffer mapped in this
+ * process, tiler_cuda_sum_exchange_buffer_bytes(rows) bytes, zeroed once);
+ * each rank waits (bounded, ~1 s; a timeout is counted in `status` and the
+ * result is NaN) for all W slots of this call and writes the fold to `out`.
+ * `seq` starts at 1 and grows by one per call, the same on every rank.
+ * world <= 8. */
+uint64_t tiler_cuda_sum_exchange_buffer_bytes(uint64_t rows);
+int32_t tiler_cuda_sum_f32_exchange(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,
+                                    const float* partial, uint64_t rows, uint32_t rank, uint32_t world,
+                                    void* const* buffers, uint32_t seq, float* out);
 /* strict_sum, evaluate.rs:498-589 (one serial fold per row). */
 int32_t tiler_cuda_strict_sum_f32(tiler_cuda_context* ctx, void* stream, const float* x,
                                   uint64_t rows, uint64_t count, float* out);

@@ -107,6 +107,17 @@ def _checks(rank, world):
         partials.append(np.float32(np.asarray(v).ravel()[0]))
     want = sharding._strict_fold(np.array(partials, np.float32))
     results["sum_rank_ordered"] = bool(np.float32(got).view(np.uint32) == np.float32(want).view(np.uint32))
+
+    # the same sum with the exchange in one kernel over NVLink, on three calls in a row
+    xch = sharding.SumExchange(1, "cuda", fam.ipc_export, fam.ipc_open, fam.ipc_close)
+    ok = True
+    for _ in range(3):
+        part = fam.sum_f32(shard, fam.plan_grouping(1, shard.numel())).reshape(1)
+        res = xch(part).cpu().numpy()
+        ok = ok and bool(res.view(np.uint32)[0] == np.float32(want).view(np.uint32))
+    torch.distributed.barrier()
+    xch.close()
+    results["sum_exchange_kernel"] = ok
     return results
 
 
@@ -140,7 +151,7 @@ def test_sharded_families_match_one_gpu(world):
     for p in procs:
         p.join(timeout=120)
     want = {"gemm_fused_allgather": True, "rms_row_shard": True, "softmax_row_shard": True,
-            "sum_rank_ordered": True}
+            "sum_rank_ordered": True, "sum_exchange_kernel": True}
     for r, res in results:
         assert isinstance(res, dict), (r, res)
         if res.pop("multicast_available"):

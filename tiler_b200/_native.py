@@ -80,6 +80,8 @@ SIGNATURES = {
     "tiler_cuda_entry_symbol": (C.c_char_p, [u32]),
     "tiler_cuda_entry_query": (i32, [P, C.c_char_p, C.POINTER(EntryProps)]),
     "tiler_cuda_module_load": (i32, [P, C.c_char_p, u64, C.POINTER(P)]),
+    "tiler_cuda_sum_exchange_buffer_bytes": (u64, [u64]),
+    "tiler_cuda_sum_f32_exchange": (i32, [P, P, P, P, u64, u32, u32, P, u32, P]),
     "tiler_cuda_module_entry": (i32, [P, C.c_char_p, C.POINTER(EntryProps)]),
     "tiler_cuda_context_bind_module": (i32, [P, P]),
     "tiler_cuda_module_launch_count": (i32, [P, C.POINTER(u64)]),

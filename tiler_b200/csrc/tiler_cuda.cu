@@ -8,3 +8,4 @@
 #include "gemm.cu"
 #include "abi.cu"
 #include "no_alloc.cu"
+#include "exchange.cu"

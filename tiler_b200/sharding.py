@@ -63,9 +63,9 @@ class PeerBlocks:
     and ``open_peer`` are the IPC calls (injected so the host logic runs
     without a GPU in tests); ``ptrs[q]`` is rank q's buffer in this process."""
 
-    def __init__(self, local: torch.Tensor, export, open_peer, close_peer=None, group=None):
+    def __init__(self, local: torch.Tensor, export, open_peer, close_peer=None, group=None, blocks=True):
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
-        assert local.dim() == 3 and local.shape[0] == self.world
+        assert not blocks or (local.dim() == 3 and local.shape[0] == self.world)
         self.local = local
         self._close = close_peer
         self._opened = []
@@ -103,6 +103,43 @@ class PeerBlocks:
             for p, offset in self._opened:
                 self._close(p, offset)
         self._opened = []
+
+
+class SumExchange:
+    """The multi-GPU sum's exchange without a library collective: each rank's
+    partial sums go into every rank's exchange buffer over NVLink (peer
+    stores) and every rank folds the W partials in rank order in one kernel
+    (``tiler_cuda_sum_f32_exchange``).  The buffers are mapped into every rank
+    once (``PeerBlocks`` over a byte buffer); ``__call__`` runs one exchange
+    and returns the [rows] result on the device."""
+
+    def __init__(self, rows: int, device, export, open_peer, close_peer=None, group=None):
+        from . import _native as N
+        self.rows = rows
+        nbytes = int(N.lib().tiler_cuda_sum_exchange_buffer_bytes(rows))
+        self.buffer = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        self.peers = PeerBlocks(self.buffer, export, open_peer, close_peer, group=group, blocks=False)
+        self.seq = 0
+
+    def __call__(self, partial: torch.Tensor, out: torch.Tensor | None = None, check: bool = True):
+        import ctypes as C
+
+        from . import _native as N
+        from . import families as F
+        self.seq += 1
+        out = torch.empty(self.rows, dtype=torch.float32, device=partial.device) if out is None else out
+        arr = (C.c_void_p * self.peers.world)(*self.peers.ptrs)
+        st = F._status() if check else None
+        F._check(N.lib().tiler_cuda_sum_f32_exchange(F.context(), F._stream(), st.ptr if st else 0,
+                                                       partial.data_ptr(), self.rows, self.peers.rank,
+                                                       self.peers.world, arr, self.seq, out.data_ptr()),
+                 "sum_f32_exchange")
+        if st:
+            F._raise_from(st, "sum_f32_exchange")
+        return out
+
+    def close(self):
+        self.peers.close()
 
 
 class MulticastBlocks:
