@@ -443,6 +443,16 @@ def family_suite(fam, torch, world, steps_small, warmup):
                     tflops * world)
     del table, ga, gas, wt, cc
     torch.cuda.empty_cache()
+    # the committed ncu summary each family's counters reproduce from
+    for name, prof in (("sum_f32_2^24", "dequantize_sum_gather_launch_metrics.txt"),
+                       ("dequantize_i8_16384x4096", "dequantize_sum_gather_launch_metrics.txt"),
+                       ("gather_bf16_8192_of_128256x4096", "dequantize_sum_gather_launch_metrics.txt"),
+                       ("silu_f32_8192x4096", "silu_f32_8192x4096.txt"),
+                       ("softmax_f32_65536x2048_causal", "softmax_f32_65536x2048_causal.txt"),
+                       ("quantize_i8_16384x4096", "quantize_i8_16384x4096.txt"),
+                       ("gemm_bf16_silu_8192x4096x14336", "gemm_bf16_silu_pair_2048x14336x4096.txt")):
+        if name in out and os.path.exists(os.path.join(ROOT, "profiles", prof)):
+            out[name]["profile"] = "profiles/" + prof
     out.update(strong_scaled_suite(fam, torch, world, steps_small, warmup))
     return out
 
