@@ -537,9 +537,9 @@ def strong_scaled_suite(fam, torch, world, steps_small, warmup):
         L.tiler_cuda_sum_f32(ctx, cur_stream(), shards[i % 4].data_ptr(), 1, s1 - s0, C.byref(gs), ws.data_ptr(),
                              ws.numel(), part.data_ptr())
         if xch is not None:
-            xch(part, out=total, check=False)
+            xch(part, out=total, check=False, device_count=True)
     if world == 1 or xch is not None:
-        ms = time_device(run_sum_xch, steps, warmup, world)
+        ms = time_device(run_sum_xch, steps, warmup, world, graph=True)
         rec("strong_sum_f32_2^24_rank_ordered", n * 4, ms, steps, f"{s1 - s0} contributors per rank")
     if xch is not None:
         torch.distributed.barrier()

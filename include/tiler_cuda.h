@@ -218,7 +218,9 @@ int32_t tiler_cuda_sum_f32_no_alloc(tiler_cuda_context* ctx, void* stream, const
  * process, tiler_cuda_sum_exchange_buffer_bytes(rows) bytes, zeroed once);
  * each rank waits (bounded, ~1 s; a timeout is counted in `status` and the
  * result is NaN) for all W slots of this call and writes the fold to `out`.
- * `seq` starts at 1 and grows by one per call, the same on every rank.
+ * `seq` starts at 1 and grows by one per call, the same on every rank; or
+ * pass 0 on every call to use the call count kept in the buffer (the same
+ * arguments then serve every call, e.g. from a captured CUDA graph).
  * world <= 8. */
 uint64_t tiler_cuda_sum_exchange_buffer_bytes(uint64_t rows);
 int32_t tiler_cuda_sum_f32_exchange(tiler_cuda_context* ctx, void* stream, tiler_cuda_status* status,

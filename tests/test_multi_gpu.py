@@ -108,12 +108,12 @@ def _checks(rank, world):
     want = sharding._strict_fold(np.array(partials, np.float32))
     results["sum_rank_ordered"] = bool(np.float32(got).view(np.uint32) == np.float32(want).view(np.uint32))
 
-    # the same sum with the exchange in one kernel over NVLink, on three calls in a row
+    # the same sum with the exchange in one kernel over NVLink, on four calls in a row
     xch = sharding.SumExchange(1, "cuda", fam.ipc_export, fam.ipc_open, fam.ipc_close)
     ok = True
-    for _ in range(3):
+    for call in range(4):
         part = fam.sum_f32(shard, fam.plan_grouping(1, shard.numel())).reshape(1)
-        res = xch(part).cpu().numpy()
+        res = xch(part, device_count=call >= 2).cpu().numpy()  # host seq 1, 2, then the buffer's count
         ok = ok and bool(res.view(np.uint32)[0] == np.float32(want).view(np.uint32))
     torch.distributed.barrier()
     xch.close()

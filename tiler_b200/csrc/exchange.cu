@@ -7,7 +7,8 @@
 //
 // Exchange buffer of each rank (caller-allocated, mapped into every rank):
 //   flags  uint32 [2][kXchMaxRanks]   seq of the call that filled each slot
-//   slots  float  [2][kXchMaxRanks][rows]
+//   count  uint32 at byte 64           calls made on this rank (seq = 0 takes count + 1)
+//   slots  float  [2][kXchMaxRanks][rows] from byte 128
 // Calls alternate between the two halves by the parity of `seq` (the caller
 // increments it by one per call, the same on every rank).  A rank reaches call
 // n + 2 only after every rank has written call n + 1, which each did after
@@ -23,7 +24,7 @@ constexpr uint32_t kXchMaxRanks = 8;
 constexpr uint64_t kXchWaitNs = 1000000000ull;
 
 __host__ __device__ __forceinline__ uint64_t xch_slot_offset(uint32_t half, uint32_t q, uint64_t row, uint64_t rows) {
-  return 64 + ((uint64_t)half * kXchMaxRanks + q) * rows * 4 + row * 4;
+  return 128 + ((uint64_t)half * kXchMaxRanks + q) * rows * 4 + row * 4;
 }
 
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
@@ -45,9 +46,19 @@ __global__ void __launch_bounds__(256) sum_exchange_kernel(const float* __restri
                                                            uint32_t seq, float* __restrict__ out,
                                                            tiler_cuda_status* st) {
   uint8_t* const* bufs = bufs_in.p;
-  const uint32_t half = seq & 1u;
   __shared__ int timed_out;
-  if (threadIdx.x == 0) timed_out = 0;
+  __shared__ uint32_t call_seq;
+  if (threadIdx.x == 0) {
+    timed_out = 0;
+    // seq 0: the call number kept in this rank's buffer, so that the same
+    // launch (captured in a CUDA graph, say) serves every call
+    uint32_t* count = reinterpret_cast<uint32_t*>(bufs[rank] + 64);
+    call_seq = seq ? seq : *count + 1;
+    *count = call_seq;
+  }
+  __syncthreads();
+  seq = call_seq;
+  const uint32_t half = seq & 1u;
   // 1. this rank's partials into slot `rank` of every rank's buffer
   for (uint64_t r = threadIdx.x; r < rows; r += blockDim.x) {
     const float v = partial[r];

@@ -121,18 +121,22 @@ class SumExchange:
         self.peers = PeerBlocks(self.buffer, export, open_peer, close_peer, group=group, blocks=False)
         self.seq = 0
 
-    def __call__(self, partial: torch.Tensor, out: torch.Tensor | None = None, check: bool = True):
+    def __call__(self, partial: torch.Tensor, out: torch.Tensor | None = None, check: bool = True,
+                 device_count: bool = False):
+        """One exchange; ``device_count`` takes the call number from the
+        buffer's own counter (seq 0), so the launch can be graph-captured."""
         import ctypes as C
 
         from . import _native as N
         from . import families as F
         self.seq += 1
+        seq = 0 if device_count else self.seq
         out = torch.empty(self.rows, dtype=torch.float32, device=partial.device) if out is None else out
         arr = (C.c_void_p * self.peers.world)(*self.peers.ptrs)
         st = F._status() if check else None
         F._check(N.lib().tiler_cuda_sum_f32_exchange(F.context(), F._stream(), st.ptr if st else 0,
                                                        partial.data_ptr(), self.rows, self.peers.rank,
-                                                       self.peers.world, arr, self.seq, out.data_ptr()),
+                                                       self.peers.world, arr, seq, out.data_ptr()),
                  "sum_f32_exchange")
         if st:
             F._raise_from(st, "sum_f32_exchange")
