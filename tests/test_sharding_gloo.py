@@ -68,6 +68,20 @@ def _worker(rank, world, port, q):
         assert calls == [(want_ptrs, rank, world)]
         assert got is blocks.local and torch.equal(got[rank], a @ w[c0:c1].t())
 
+        # the multicast form's host logic: one call with this rank's buffer and its
+        # multicast address, between the two ordering all-reduces (gloo here)
+        import types
+        mb = types.SimpleNamespace(local=torch.zeros(world, m, c1 - c0), local_ptr=11, multicast_ptr=22,
+                                   rank=rank, world=world)
+        mcalls = []
+
+        def fused_mc(aa, ww, lp, mp, r, nw):
+            mcalls.append((lp, mp, r, nw))
+            mb.local[r] = aa @ ww.t()
+        got = sharding.gemm_n_sharded_multicast(a, w[c0:c1].contiguous(), mb, fused_mc)
+        assert mcalls == [(11, 22, rank, world)] and got is mb.local
+        assert torch.equal(got[rank], a @ w[c0:c1].t())
+
         # a mapping failure on one rank is raised on every rank alike
         def export_fails_on_1(t):
             if rank == 1:
