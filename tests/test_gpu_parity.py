@@ -235,6 +235,24 @@ def test_rms_norm_bf16_matches_oracle(fam, oracle_lib, rows, extent):
     assert (got == want).all(), f"{(got != want).sum()} bf16 mismatches"
 
 
+@pytest.mark.parametrize("extent,eps_bits", [(1, 1), (1, 0x358637BD), (4, 1), (4, 0x358637BD)])
+def test_rms_norm_scale_sweeps_the_certified_rsqrt(fam, oracle_lib, extent, eps_bits):
+    """Millions of rows whose mean square t spans every binade (subnormal t,
+    overflow to +inf included), so the certified reciprocal square root of
+    the row scale is decided against the oracle's over ~2^21 distinct t."""
+    rows = 1 << 21
+    rng = np.random.default_rng(extent * 7 + eps_bits % 97)
+    mant = rng.integers(0, 1 << 23, rows * extent, dtype=np.uint32)
+    expo = rng.integers(127 - 80, 127 + 70, rows * extent, dtype=np.uint32)
+    sign = rng.integers(0, 2, rows * extent, dtype=np.uint32) << 31
+    x = (sign | (expo << 23) | mant).view(np.float32).reshape(rows, extent)
+    w = np.ones(extent, np.float32)
+    got = host(fam.rms_norm(cuda(x), cuda(w), eps_bits=eps_bits))
+    st, want = oracle_lib.rms_norm_f32(x, w, eps_bits=eps_bits, nthreads=16)
+    assert st == 0
+    assert_bits_equal(got, want, f"rms f32 rsqrt sweep extent {extent} eps {eps_bits:#x}")
+
+
 def _fold_stress_rows(seed, rows, extent):
     """Rows that drive the warp-cooperative strict fold of the squares through
     every event it has: binade crossings from tiny first squares, exact ties

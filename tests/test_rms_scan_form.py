@@ -1,6 +1,6 @@
-"""The warp-per-row RMS form (rms_scan.cu, selected with TILER_RMS_FORM=scan,
-read once per process) held to the same parity tests as the default wave
-form: the RMS f32 / bf16 oracle cases at full and ragged sizes, the fold
+"""The other RMS forms -- warp-per-row (rms_scan.cu, TILER_RMS_FORM=scan) and
+chunk-streamed (rms_stream.cu, TILER_RMS_FORM=stream), the variable read once
+per process -- held to the same parity tests as the default wave form: the RMS f32 / bf16 oracle cases at full and ragged sizes, the fold
 stress rows (ties, binade crossings, tiny and overflowing sums, NaN / inf) and
 the fused quantize, run in a child process with the form selected."""
 import os
@@ -15,10 +15,11 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def test_scan_form_passes_the_rms_parity_tests():
+@pytest.mark.parametrize("form", ["scan", "stream"])
+def test_rms_form_passes_the_rms_parity_tests(form):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
-    env = dict(os.environ, TILER_RMS_FORM="scan")
+    env = dict(os.environ, TILER_RMS_FORM=form)
     sel = "rms_norm_f32_matches or rms_norm_bf16_matches or fold_stress or quantize_fusion"
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-m", "gpu", "-p", "no:cacheprovider",
                         os.path.join(ROOT, "tests", "test_gpu_parity.py"), "-k", sel],

@@ -310,7 +310,17 @@ __device__ __forceinline__ float rsqrt_cr(float t) {
   if (isinf(t)) return t > 0 ? 0.0f : __uint_as_float(kCanonicalNan);
   if (t == 0.0f) return signbit(t) ? __uint_as_float(0xff800000u) : __uint_as_float(0x7f800000u);
   if (t < 0.0f) return __uint_as_float(kCanonicalNan);
-  float f = __double2float_rn(__drcp_rn(__dsqrt_rn((double)t)));
+  // candidate: the hardware reciprocal square root (relative error below
+  // 2^-21) refined by one Newton step in binary64, r1 = r0 + (r0/2)(1 - t r0^2),
+  // which leaves it within 2^-40 of 1/sqrt(t); a subnormal t is first scaled
+  // by 2^64 (exact) and the result by 2^32.  The exact midpoint test below
+  // decides the rounding whatever the candidate's error.
+  const bool tiny = t < 0x1p-126f;
+  const float ts = tiny ? t * 0x1p64f : t;
+  const double r0 = (double)rsqrtf(ts);
+  const double e = __fma_rn(-__dmul_rn((double)ts, r0), r0, 1.0);
+  const double r1 = __fma_rn(__dmul_rn(0.5, r0), e, r0);
+  float f = __double2float_rn(tiny ? r1 * 0x1p32 : r1);
   for (int it = 0; it < 4; ++it) {
     double fd = f;
     double mhi = 0.5 * (fd + (double)next_up(f));
@@ -402,6 +412,11 @@ __device__ __forceinline__ uint4 lds_u4(uint32_t saddr) {
   return v;
 }
 
+__device__ __forceinline__ void sts_u4(uint32_t saddr, const uint4& v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(saddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -463,6 +478,16 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
   asm volatile(
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
           smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// The same with the destination as a shared-window address.
+__device__ __forceinline__ void bulk_g2s_u32(uint32_t smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_dst),
       "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }

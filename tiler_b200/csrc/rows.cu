@@ -523,18 +523,21 @@ __global__ void rms_norm_generic_kernel(const void* __restrict__ xv, const void*
   }
 }
 
-// TILER_RMS_FORM=scan in the environment (read once per process) selects the
-// warp-per-row kernel (rms_scan.cu) where it applies: exact as well, and
-// measured slower than the wave kernel at the BASELINE shapes (its per-row
-// fold is latency-bound with 12 rows in flight per SM), so the wave kernel is
-// the default.
-static bool rms_scan_form_selected() {
-  static const bool scan = [] {
+// TILER_RMS_FORM in the environment (read once per process) selects the RMS
+// kernel where it applies: "scan" the warp-per-row kernel (rms_scan.cu),
+// "stream" the chunk-streamed kernel (rms_stream.cu), "wave" the wave kernel.
+// All are exact; the default is the wave kernel.
+enum RmsForm { kRmsFormWave = 0, kRmsFormScan = 1, kRmsFormStream = 2 };
+static int rms_form_selected() {
+  static const int form = [] {
     const char* v = getenv("TILER_RMS_FORM");
-    return v && strcmp(v, "scan") == 0;
+    if (v && strcmp(v, "scan") == 0) return (int)kRmsFormScan;
+    if (v && strcmp(v, "stream") == 0) return (int)kRmsFormStream;
+    return (int)kRmsFormWave;
   }();
-  return scan;
+  return form;
 }
+static bool rms_scan_form_selected() { return rms_form_selected() == kRmsFormScan; }
 
 int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_stride, uint64_t rows,
                                 uint64_t extent, float eps, int8_t* codes, float* scales, tiler_cuda_status* st,
@@ -574,6 +577,9 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
   // weights, rows up to 16 KB)
   if (rms_scan_form_selected() &&
       rms_scan_launch(bf16, 0, x, w, w_row_stride, rows, extent, eps, y, nullptr, nullptr, st, sm_count, stream))
+    return 0;
+  if (rms_form_selected() == kRmsFormStream &&
+      rms_stream_launch(bf16, x, w, w_row_stride, rows, extent, eps, y, st, sm_count, stream))
     return 0;
   // One CTA per SM; each takes rows/grid consecutive rows in waves.
   const uint64_t grid = umin64((uint64_t)sm_count, rows);

@@ -4,6 +4,7 @@
 #include "reduce.cu"
 #include "rows.cu"
 #include "rms_scan.cu"
+#include "rms_stream.cu"
 #include "maps.cu"
 #include "gemm.cu"
 #include "abi.cu"
