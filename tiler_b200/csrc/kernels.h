@@ -51,6 +51,9 @@ bool rms_scan_launch(int bf16, int quant, const void* x, const void* w, int64_t 
 // chunk rings hold).
 bool rms_stream_launch(int bf16, const void* x, const void* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,
                        float eps, void* y, tiler_cuda_status* st, int sm_count, cudaStream_t stream);
+bool rms_stream_quant_launch(const float* x, const float* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,
+                             float eps, int8_t* codes, float* scales, tiler_cuda_status* st, int sm_count,
+                             cudaStream_t stream);
 void launch_bounded_wait_selftest(tiler_cuda_status* st, uint64_t limit_ns, cudaStream_t stream);
 void launch_quantize_i8_rows(const float* x, uint64_t rows, uint64_t extent, int8_t* codes, float* scales,
                              tiler_cuda_status* st, int sm_count, cudaStream_t stream);

@@ -68,6 +68,10 @@ struct RmsStreamSmem {
   uint64_t folded[Cfg::kRing];     // group t: its scales are known
   uint64_t normalized[Cfg::kRing]; // group t: its chunk slots are free
   float sum[Cfg::kRing][Cfg::R];  // group t's sums of squares
+  // fused quantize: per row of group t, the largest |y| (magnitude bits) and
+  // the first column whose y is NaN, combined over the normalize warps
+  uint32_t ymax[Cfg::kRing][Cfg::R];
+  uint32_t ynan[Cfg::kRing][Cfg::R];
   alignas(128) uint8_t buf[Cfg::kBuffers * Cfg::kPitch];
 };
 template <class Cfg>
@@ -165,10 +169,15 @@ __device__ __forceinline__ float rms_fold_chunk(float acc, uint32_t p, uint32_t 
   return acc;
 }
 
-template <class E, class Cfg>
+// QUANT: the fused RMS norm -> per-row int8 quantize (f32 only): the
+// normalize warps keep y in registers, combine each row's max |y| across
+// the chunk owners (shared-memory atomics and one named barrier per group)
+// and write the codes and scales; y never leaves the SM.
+template <class E, class Cfg, bool QUANT = false>
 __device__ __forceinline__ void rms_norm_stream(const uint8_t* __restrict__ x, const uint8_t* __restrict__ w,
                                                 uint64_t rows, uint64_t extent, float eps, uint8_t* __restrict__ y,
-                                                tiler_cuda_status* st) {
+                                                tiler_cuda_status* st, int8_t* __restrict__ codes = nullptr,
+                                                float* __restrict__ scales = nullptr) {
   constexpr int P = Cfg::P, R = Cfg::R, C = Cfg::C, RING = Cfg::kRing, PITCH = Cfg::kPitch;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   RmsStreamSmem<Cfg>& S = *reinterpret_cast<RmsStreamSmem<Cfg>*>(smem_raw);
@@ -253,7 +262,13 @@ __device__ __forceinline__ void rms_norm_stream(const uint8_t* __restrict__ x, c
       // normalize warps, which form the scales off the chain's path
       const int tf = b - (nch - 1);
       if (tf >= 0 && tf < G) {
-        if (valid && k == nch - 1) S.sum[tf % RING][r] = acc;
+        if (valid && k == nch - 1) {
+          S.sum[tf % RING][r] = acc;
+          if constexpr (QUANT) {
+            S.ymax[tf % RING][r] = 0;
+            S.ynan[tf % RING][r] = 0xffffffffu;
+          }
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.folded[tf % RING]);
       }
@@ -276,28 +291,157 @@ __device__ __forceinline__ void rms_norm_stream(const uint8_t* __restrict__ x, c
       if (!mbar_wait(&S.folded[t % RING], (uint32_t)((t / RING) & 1), st)) break;
       const int gr = group_rows(t);
       const uint32_t slot_off = (uint32_t)((t % lkk) * R * PITCH);
-      for (int rr = 0; kk < nch && rr < gr; ++rr) {
-        // rms_norm.rs:172-193: mean = total / N, t = mean + eps, certified rsqrt
-        const float s = rsqrt_cr(__fadd_rn(__fdiv_rn(S.sum[t % RING][rr], (float)extent), eps));
-        const uint32_t p = ring_base(kk, rr) + slot_off;
-        uint4* yk = reinterpret_cast<uint4*>(y + (rb + (uint64_t)t * R + rr) * row_bytes + off);
-        uint4 xq[U];
+      // rms_norm.rs:172-193: mean = total / N, t = mean + eps, certified rsqrt;
+      // lane r forms row r's scale
+      const float s_lane =
+          lane < gr ? rsqrt_cr(__fadd_rn(__fdiv_rn(S.sum[t % RING][lane], (float)extent), eps)) : 0.0f;
+      if constexpr (QUANT) {
+        // quantize_i8_rows of each row's y (quantization.rs:188-247, :404-430
+        // with the per-row scale max|y| / 127): y stays in registers between
+        // the maximum and the codes; the group's rows are handled together
+        // (unrolled) so their dependent steps overlap
+        float yr[R][U][E::kPerVec];
+        uint32_t mb[R], first[R];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (lane + 32 * u < nvec) xq[u] = lds_u4_nv(p + (lane + 32 * u) * 16);
+        for (int rr = 0; rr < R; ++rr) {
+          mb[rr] = 0;
+          first[rr] = 0xffffffffu;
+          if (kk < nch && rr < gr) {
+            const float s = __shfl_sync(0xffffffffu, s_lane, rr);
+            const uint32_t p = ring_base(kk, rr) + slot_off;
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (lane + 32 * u < nvec) {
-            float xe[E::kPerVec], we[E::kPerVec], ye[E::kPerVec];
-            E::unpack(xq[u], xe);
-            E::unpack(wq[u], we);
+            for (int u = 0; u < U; ++u)
+              if (lane + 32 * u < nvec) {
+                float xe[E::kPerVec], we[E::kPerVec];
+                E::unpack(lds_u4_nv(p + (lane + 32 * u) * 16), xe);
+                E::unpack(wq[u], we);
 #pragma unroll
-            for (int j = 0; j < E::kPerVec; ++j) {
-              const float yv = __fmul_rn(we[j], __fmul_rn(xe[j], s));
-              ye[j] = E::kPackCanonicalizes ? yv : canon(yv);
-            }
-            st_global_stream_u4(yk + lane + 32 * u, E::pack(ye));
+                for (int j = 0; j < E::kPerVec; ++j) {
+                  // a NaN y (any payload) has magnitude bits above +inf's
+                  const float yv = __fmul_rn(we[j], __fmul_rn(xe[j], s));
+                  yr[rr][u][j] = yv;
+                  mb[rr] = max(mb[rr], __float_as_uint(yv) & 0x7fffffffu);
+                }
+              }
           }
+        }
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          const uint32_t m = __reduce_max_sync(0xffffffffu, mb[rr]);
+          if (m > 0x7f800000u) {  // the chunk holds a NaN y: its first column
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+              for (int j = 0; j < E::kPerVec; ++j)
+                if (lane + 32 * u < nvec && (__float_as_uint(yr[rr][u][j]) & 0x7fffffffu) > 0x7f800000u)
+                  first[rr] = min(first[rr], (uint32_t)(off / sizeof(float)) + (lane + 32 * u) * E::kPerVec + j);
+          }
+          const uint32_t f = __reduce_min_sync(0xffffffffu, first[rr]);
+          if (lane == 0 && kk < nch && rr < gr) {
+            atomicMax(&S.ymax[t % RING][rr], m);
+            if (f != 0xffffffffu) atomicMin(&S.ynan[t % RING][rr], f);
+          }
+        }
+        // y is in registers: the group's chunk slots can be refilled while the
+        // codes are formed
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.normalized[t % RING]);
+        // every normalize warp has combined its chunk of every row
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * kRmsStreamNormWarps) : "memory");
+        // lane r forms row r's quantize scale max|y| / 127 and its reciprocal
+        const uint32_t mb_lane = lane < gr ? S.ymax[t % RING][lane] : 0u;
+        float scale_lane = 0.0f, inv_lane = 0.0f;
+        if (lane < gr) {
+          scale_lane = __fdiv_rn(__uint_as_float(mb_lane), 127.0f);
+          if (is_positive_normal(scale_lane)) inv_lane = __frcp_rn(scale_lane);
+        }
+        if (nw == 0 && lane < gr) {
+          const uint64_t row = rb + (uint64_t)t * R + lane;
+          if (mb_lane > 0x7f800000u) {  // a NaN y: report its first column
+            report_error(st, row * extent + S.ynan[t % RING][lane], TILER_CUDA_NAN_INPUT);
+          } else {
+            scales[row] = scale_lane;
+            if (!is_positive_normal(scale_lane)) report_error(st, row * extent, TILER_CUDA_SCALE_DOMAIN);
+          }
+        }
+        // code = rint(y / scale) clamped to [-127, 127]: y * (1/scale) decides
+        // it unless the product lies within 3e-5 of a half-integer, where the
+        // exact quotient is taken (one warp-uniform branch).  |q| <= 127, so
+        // RN(q + 1.5 * 2^23) is 1.5 * 2^23 + rint(q) (ties to even), whose
+        // low bits are the integer
+        constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+        float scale[R], inv[R];
+        bool live[R];
+        float tv[R][U][4];
+        bool near_half = false;
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          const uint32_t m = __shfl_sync(0xffffffffu, mb_lane, rr);
+          scale[rr] = __shfl_sync(0xffffffffu, scale_lane, rr);
+          inv[rr] = __shfl_sync(0xffffffffu, inv_lane, rr);
+          live[rr] = kk < nch && rr < gr && m <= 0x7f800000u && is_positive_normal(scale[rr]);
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float q = __fmul_rn(yr[rr][u][j], inv[rr]);
+              const float t1 = __fadd_rn(q, kMagic);
+              near_half |= live[rr] && lane + 32 * u < nvec && fabsf(__fsub_rn(q, __fsub_rn(t1, kMagic))) > 0.49997f;
+              tv[rr][u][j] = t1;
+            }
+        }
+        if (__any_sync(0xffffffffu, near_half)) {
+#pragma unroll
+          for (int rr = 0; rr < R; ++rr)
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float q = __fmul_rn(yr[rr][u][j], inv[rr]);
+                if (live[rr] && fabsf(__fsub_rn(q, __fsub_rn(tv[rr][u][j], kMagic))) > 0.49997f)
+                  tv[rr][u][j] = __fadd_rn(__fdiv_rn(yr[rr][u][j], scale[rr]), kMagic);
+              }
+        }
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          if (!live[rr]) continue;
+          int* crow = reinterpret_cast<int*>(codes + (rb + (uint64_t)t * R + rr) * extent + off / sizeof(float));
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (lane + 32 * u < nvec) {
+              int c[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) c[j] = max(-127, min(127, (int)__float_as_uint(tv[rr][u][j]) - 0x4B400000));
+              uint32_t hi, packed;  // cvt.pack d, a, b, c: d = c << 16 | sat8(a) << 8 | sat8(b)
+              asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(hi) : "r"(c[3]), "r"(c[2]));
+              asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(packed) : "r"(c[1]), "r"(c[0]), "r"(hi));
+              __stcs(crow + lane + 32 * u, (int)packed);
+            }
+        }
+        continue;  // the slots were released above
+      } else {
+        for (int rr = 0; kk < nch && rr < gr; ++rr) {
+            const float s = __shfl_sync(0xffffffffu, s_lane, rr);
+          const uint32_t p = ring_base(kk, rr) + slot_off;
+          uint4* yk = reinterpret_cast<uint4*>(y + (rb + (uint64_t)t * R + rr) * row_bytes + off);
+          uint4 xq[U];
+  #pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (lane + 32 * u < nvec) xq[u] = lds_u4_nv(p + (lane + 32 * u) * 16);
+  #pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (lane + 32 * u < nvec) {
+              float xe[E::kPerVec], we[E::kPerVec], ye[E::kPerVec];
+              E::unpack(xq[u], xe);
+              E::unpack(wq[u], we);
+  #pragma unroll
+              for (int j = 0; j < E::kPerVec; ++j) {
+                const float yv = __fmul_rn(we[j], __fmul_rn(xe[j], s));
+                ye[j] = E::kPackCanonicalizes ? yv : canon(yv);
+              }
+              st_global_stream_u4(yk + lane + 32 * u, E::pack(ye));
+            }
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.normalized[t % RING]);
@@ -317,6 +461,13 @@ extern "C" __global__ void __launch_bounds__(tc::RmsStreamF32::kThreads, 1)
 extern "C" __global__ void __launch_bounds__(tc::RmsStreamBF16::kThreads, 1)
     tiler_rms_norm_stream_bf16(TILER_RMS_STREAM_PARAMS) {
   tc::rms_norm_stream<tc::RmsElem<true>, tc::RmsStreamBF16>(x, w, rows, extent, eps, y, st);
+}
+extern "C" __global__ void __launch_bounds__(tc::RmsStreamF32::kThreads, 1)
+    tiler_rms_norm_stream_quantize_i8(const uint8_t* __restrict__ x, const uint8_t* __restrict__ w, uint64_t rows,
+                                      uint64_t extent, float eps, int8_t* __restrict__ codes,
+                                      float* __restrict__ scales, tiler_cuda_status* st) {
+  tc::rms_norm_stream<tc::RmsElem<false>, tc::RmsStreamF32, true>(x, w, rows, extent, eps, nullptr, st, codes,
+                                                                 scales);
 }
 #undef TILER_RMS_STREAM_PARAMS
 
@@ -339,6 +490,23 @@ bool rms_stream_launch(int bf16, const void* x, const void* w, int64_t w_row_str
   launch_kernel(fn, bf16 ? "tiler_rms_norm_stream_bf16" : "tiler_rms_norm_stream_f32", dim3((unsigned)grid),
                 dim3(RmsStreamF32::kThreads), smem, stream, (const uint8_t*)x, (const uint8_t*)w, rows, extent, eps,
                 (uint8_t*)y, st);
+  return true;
+}
+
+// The fused RMS -> int8 quantize in the streamed form (f32 rows of up to
+// 16 KB, a broadcast weight row); false where it does not apply.
+bool rms_stream_quant_launch(const float* x, const float* w, int64_t w_row_stride, uint64_t rows, uint64_t extent,
+                             float eps, int8_t* codes, float* scales, tiler_cuda_status* st, int sm_count,
+                             cudaStream_t stream) {
+  const uint64_t row_bytes = extent * 4;
+  if (w_row_stride != 0 || row_bytes % 16 || row_bytes > (uint64_t)RmsStreamF32::P * RmsStreamF32::CB) return false;
+  const uint64_t grid = umin64((uint64_t)sm_count, rows);
+  if (rows / grid >= (1ull << 30)) return false;
+  const size_t smem = rms_stream_smem_bytes<RmsStreamF32>();
+  cudaFuncSetAttribute(tiler_rms_norm_stream_quantize_i8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_kernel((const void*)tiler_rms_norm_stream_quantize_i8, "tiler_rms_norm_stream_quantize_i8",
+                dim3((unsigned)grid), dim3(RmsStreamF32::kThreads), smem, stream, (const uint8_t*)x,
+                (const uint8_t*)w, rows, extent, eps, codes, scales, st);
   return true;
 }
 

@@ -549,6 +549,9 @@ int launch_rms_norm_quantize_i8(const float* x, const float* w, int64_t w_row_st
   if (rms_scan_form_selected() &&
       rms_scan_launch(0, 1, x, w, w_row_stride, rows, extent, eps, nullptr, codes, scales, st, sm_count, stream))
     return 0;
+  if (rms_form_selected() == kRmsFormStream &&
+      rms_stream_quant_launch(x, w, w_row_stride, rows, extent, eps, codes, scales, st, sm_count, stream))
+    return 0;
   const uint64_t grid = umin64((uint64_t)sm_count, rows);
   cudaFuncSetAttribute(tiler_rms_norm_wave_quantize_i8, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)kRmsSmemBytes);
