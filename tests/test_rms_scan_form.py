@@ -1,8 +1,9 @@
-"""The other RMS forms -- warp-per-row (rms_scan.cu, TILER_RMS_FORM=scan) and
-chunk-streamed (rms_stream.cu, TILER_RMS_FORM=stream), the variable read once
-per process -- held to the same parity tests as the default wave form: the RMS f32 / bf16 oracle cases at full and ragged sizes, the fold
-stress rows (ties, binade crossings, tiny and overflowing sums, NaN / inf) and
-the fused quantize, run in a child process with the form selected."""
+"""Every RMS form, selected with TILER_RMS_FORM (read once per process) --
+warp-per-row (rms_scan.cu, "scan"), chunk-streamed (rms_stream.cu, "stream"),
+wave ("wave") -- held to the same parity tests the default selection passes:
+the RMS f32 / bf16 oracle cases at full and ragged sizes, the fold stress rows
+(ties, binade crossings, tiny and overflowing sums, NaN / inf) and the fused
+quantize, run in a child process with the form selected."""
 import os
 import subprocess
 import sys
@@ -15,7 +16,7 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("form", ["scan", "stream"])
+@pytest.mark.parametrize("form", ["scan", "stream", "wave"])
 def test_rms_form_passes_the_rms_parity_tests(form):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")

@@ -25,9 +25,10 @@
 #include "drv.cuh"
 
 // Kernels a payload module may carry, by C name.
-constexpr int kModuleKernelCount = 12;
+constexpr int kModuleKernelCount = 15;
 inline const char* const kModuleKernels[kModuleKernelCount] = {
     "tiler_rms_norm_wave_f32", "tiler_rms_norm_wave_bf16", "tiler_rms_norm_wave_quantize_i8",
+    "tiler_rms_norm_stream_f32", "tiler_rms_norm_stream_bf16", "tiler_rms_norm_stream_quantize_i8",
     "tiler_rms_norm_f32",   "tiler_rms_norm_bf16",  "tiler_rms_norm_quantize_i8",
     "tiler_grouped_sum_k1", "tiler_grouped_sum_k2", "tiler_grouped_sum_k4",
     "tiler_grouped_max_k1", "tiler_grouped_max_k2", "tiler_grouped_max_k4",
