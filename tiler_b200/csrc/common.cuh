@@ -264,29 +264,49 @@ __device__ __forceinline__ float exp_cr_fast(float x, const double* table_hi, ti
 
 // exp_cr_fast without its fallback, for callers that batch the rare
 // undecided arguments into one warp-uniform branch: returns the binary32
-// bits of e^x and sets *ok when they are certified (normal binary32 result,
-// binary64 value farther than 64 units of 2^-46 from a rounding midpoint);
-// otherwise the caller must take exp_cr(x).  The rounding to binary32 is
-// done on the bits: the candidate is 29 bits beyond binary32 precision and
-// not at a midpoint, so bit 28 of the low word decides it.
+// bits of e^x for x in (-104, 89) and sets *ok when they are certified;
+// otherwise the caller must take exp_cr(x).  A leaner evaluation than
+// exp_cr_fast's, with the certification window widened to match:
+//   n = rint(x * 256/ln2) (one FMA against 1.5 * 2^52), j = n mod 256,
+//   r = x - n * L with L = RN(ln2/256), one FMA (|r| <= ln2/512 + tiny);
+//     |n| < 2^15.3 and |L - ln2/256| <= 2^-62 put r within 2^-46.7 of
+//     x - n ln2/256;
+//   e^r - 1 ~ r + r^2 (1/2 + r/6), truncation below |r|^4/24 < 2^-42.7;
+//   y = 2^(j/256) (1 + p), the table entry and the FMA rounding add 2^-52;
+// so y is within 2^-42.6 (relative) of e^x, i.e. within 2^10.4 units of
+// its own last bit.  It is certified when it is a normal binary32 value
+// (hi in [0x38100000, 0x47f00000)) and its 29 bits below binary32 precision
+// lie more than 2048 units from the midpoint pattern 1 << 28; then bit 28
+// of the low word rounds it.  A value within the window (about one in 2^17)
+// takes the caller's exact path.
+#ifndef TILER_EXP_LEAN
+#define TILER_EXP_LEAN 1
+#endif
+constexpr double kLn2By256 = 0x1.62e42fefa39efp-9;  // RN(ln2 / 256)
 __device__ __forceinline__ uint32_t exp_cr_bits(float x, const double* table_hi, bool* ok) {
   const double xd = (double)x;
   const double t = __fma_rn(xd, kInvLn2x256, kRoundShift);
   const int n = __double2loint(t);
   const double nd = __dsub_rn(t, kRoundShift);
+#if TILER_EXP_LEAN
+  const double r = __fma_rn(-nd, kLn2By256, xd);
+  const double q = __fma_rn(r, 1.0 / 6.0, 0.5);
+  const double p = __fma_rn(__dmul_rn(r, r), q, r);
+  constexpr uint32_t kWindow = 2048;
+#else
   double r = __fma_rn(-nd, kLn2By256Hi, xd);
   r = __fma_rn(-nd, kLn2By256Mid, r);
   double q = __fma_rn(r, 1.0 / 24.0, 1.0 / 6.0);
   q = __fma_rn(r, q, 0.5);
   const double p = __fma_rn(__dmul_rn(r, r), q, r);
+  constexpr uint32_t kWindow = 64;
+#endif
   const double tj = table_hi[n & 255];
   const double y0 = __fma_rn(tj, p, tj);
   const uint32_t hi = (uint32_t)__double2hiint(y0) + ((uint32_t)(n >> 8) << 20);
   const uint32_t lo = (uint32_t)__double2loint(y0);
-  // normal binary32 range: hi in [0x38100000, 0x47f00000); not within 64
-  // units of the midpoint pattern 1 << 28 in the low 29 bits
   *ok = (hi - 0x38100000u) < (0x47f00000u - 0x38100000u) &&
-        ((lo & 0x1fffffffu) - (0x10000000u - 64u)) > 128u;
+        ((lo & 0x1fffffffu) - (0x10000000u - kWindow)) > 2 * kWindow;
   // binary32 bits: exponent rebased, 23 mantissa bits from hi:lo, rounded by bit 28
   return __funnelshift_l(lo, hi - 0x38000000u, 3) + ((lo >> 28) & 1u);
 }

@@ -648,6 +648,207 @@ __device__ __noinline__ float softmax_exp_slow(float sh, const double* table, ti
   return sh > -104.0f ? exp_cr(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
 }
 
+// Step 2 of the softmax kernels for one row: with a mask tensor, t = x + mask
+// in place; the row maximum over the unmasked columns; e_i = exp(x_i - m) in
+// place (masked columns zero-filled); the row's poison flag and the end of its
+// denominator fold go to *poisoned_out and *fold_end_out (lane 0).
+__device__ __forceinline__ void softmax_row_exp(float* b, uint64_t row, uint32_t lane, uint64_t extent, bool causal,
+                                                uint64_t period, uint64_t row_offset, const float* __restrict__ mask,
+                                                uint64_t mask_rows, const double* table, tiler_cuda_status* st,
+                                                uint32_t* poisoned_out, uint32_t* fold_end_out) {
+  const uint32_t ext = (uint32_t)extent;
+  const uint32_t live = causal ? (uint32_t)umin64((row_offset + row) % period + 1, extent) : ext;
+  float4* b4 = reinterpret_cast<float4*>(b);
+  float m = __uint_as_float(0xff800000u);
+  const uint32_t live4 = live / 4;
+  if (mask) {
+    // the program's additive mask (an add-f32 of a broadcast mask tensor,
+    // standard.rs:211-221): t = x + mask[row mod mask_rows], one rounding,
+    // NaN canonicalized, written back in place before the maximum
+    const float4* m4 = reinterpret_cast<const float4*>(mask + ((row_offset + row) % mask_rows) * extent);
+    for (uint32_t v = lane; v < live4; v += 32) {
+      const float4 q = b4[v], a = __ldg(m4 + v);
+      const float4 t = make_float4(canon(__fadd_rn(q.x, a.x)), canon(__fadd_rn(q.y, a.y)),
+                                   canon(__fadd_rn(q.z, a.z)), canon(__fadd_rn(q.w, a.w)));
+      b4[v] = t;
+      m = max_nan(max_nan(m, t.x), max_nan(t.y, max_nan(t.z, t.w)));
+    }
+  } else {
+    for (uint32_t v = lane; v < live4; v += 32) {
+      const float4 q = b4[v];
+      m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
+    }
+  }
+  for (uint32_t c = live4 * 4 + lane; c < live; c += 32) m = max_nan(m, b[c]);
+  uint32_t bad = 0;  // a masked x that is NaN or +inf poisons the row
+  const uint32_t mask4 = (live + 3) / 4;  // first whole masked vector
+  auto poison = [](uint32_t xb) { return (uint32_t)(((xb & 0x7fffffffu) > 0x7f800000u) | (xb == 0x7f800000u)); };
+  for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) bad |= poison(__float_as_uint(b[c]));
+  for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) {
+    const uint4 q = reinterpret_cast<const uint4*>(b)[v];
+    bad |= poison(q.x) | poison(q.y) | poison(q.z) | poison(q.w);
+  }
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+  bad = __any_sync(0xffffffffu, bad != 0);
+  // m is -inf only if every unmasked x is -inf: x - m is then NaN
+  auto exp_of = [&](float xv) {
+    const float sh = __fsub_rn(xv, m);
+    return sh > -104.0f ? exp_cr_fast(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
+  };
+  uint32_t last_nz = 0;  // one past this lane's last nonzero e (mask tensor only)
+  // TRACK (a mask tensor): arguments at or below -104 give +0 without
+  // certification and the last nonzero e is tracked, so the fold can stop
+  // there; the in-kernel causal mask already stops at the diagonal
+  auto exp_pass = [&](auto track) {
+    constexpr bool TRACK = decltype(track)::value;
+    constexpr int EV = TILER_SMX_EXP_VECS;  // float4s per lane per step: 4 * EV independent exps
+    for (uint32_t v0 = lane; v0 < live4; v0 += 32 * EV) {
+      float xs[4 * EV];
+      uint32_t e[4 * EV], flagged = 0;
+#pragma unroll
+      for (int h = 0; h < EV; ++h) {
+        const uint32_t v = v0 + 32 * h;
+        const float4 q = v < live4 ? b4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+        xs[4 * h] = q.x; xs[4 * h + 1] = q.y; xs[4 * h + 2] = q.z; xs[4 * h + 3] = q.w;
+      }
+      if (TRACK) {
+        // a step whose arguments are all at or below -104 (a masked stretch)
+        // is +0 throughout: skip the evaluation when the whole warp agrees
+        bool low = true;
+#pragma unroll
+        for (int i = 0; i < 4 * EV; ++i) {
+          const float sh = __fsub_rn(xs[i], m);
+          low = low && !(sh > -104.0f) && !is_nan_bits(sh);
+        }
+        if (__all_sync(__activemask(), low)) {
+#pragma unroll
+          for (int h = 0; h < EV; ++h) {
+            const uint32_t v = v0 + 32 * h;
+            if (v < live4) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          }
+          continue;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4 * EV; ++i) {
+        const float sh = __fsub_rn(xs[i], m);
+        bool ok;
+        e[i] = exp_cr_bits(sh, table, &ok);
+        if (TRACK) {
+          // e^sh = +0 for sh <= -104 (silu.rs:224-235 guards): no certification needed
+          const bool zero = !(sh > -104.0f) && !is_nan_bits(sh);
+          if (zero) e[i] = 0u;
+          flagged |= ((ok && sh > -104.0f) || zero ? 0u : 1u) << i;
+        } else {
+          flagged |= ((ok && sh > -104.0f) ? 0u : 1u) << i;
+        }
+      }
+      if (__any_sync(__activemask(), flagged != 0)) {  // rare: certify or special-case the flagged ones
+#pragma unroll
+        for (int i = 0; i < 4 * EV; ++i)
+          if ((flagged >> i) & 1u) e[i] = __float_as_uint(softmax_exp_slow(__fsub_rn(xs[i], m), table, st));
+      }
+#pragma unroll
+      for (int h = 0; h < EV; ++h) {
+        const uint32_t v = v0 + 32 * h;
+        if (v < live4) {
+          b4[v] = make_float4(__uint_as_float(e[4 * h]), __uint_as_float(e[4 * h + 1]),
+                              __uint_as_float(e[4 * h + 2]), __uint_as_float(e[4 * h + 3]));
+          if (TRACK) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (e[4 * h + i] != 0u) last_nz = max(last_nz, v * 4 + i + 1);
+          }
+        }
+      }
+    }
+  };
+  if (mask) exp_pass(std::true_type{});
+  else exp_pass(std::false_type{});
+  for (uint32_t c = live4 * 4 + lane; c < live; c += 32) {
+    b[c] = exp_of(b[c]);
+    if (mask && __float_as_uint(b[c]) != 0u) last_nz = max(last_nz, c + 1);
+  }
+  for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) b[c] = 0.0f;
+  for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (mask) last_nz = __reduce_max_sync(0xffffffffu, last_nz);
+  if (lane == 0) {
+    *poisoned_out = bad;
+    *fold_end_out = mask ? max(last_nz, 1u) : live;  // at least e_0, the seed
+  }
+}
+
+// Step 3: lane r < n folds row r's denominator strictly,
+// d = (((e_0 + e_1) + e_2) + ...) up to fold_end[r], and stores r = 1/d (NaN
+// for a poisoned row) in rcp[r].
+__device__ __forceinline__ void softmax_chain_fold(uint32_t lane, uint32_t n, const float* bufs, uint32_t ext,
+                                                   const uint32_t* fold_end, const uint32_t* poisoned, float* rcp) {
+  if (lane < n) {
+    const uint32_t live = fold_end[lane];  // the unmasked columns up to the last nonzero e
+    const uint32_t base = smem_u32(bufs + (uint64_t)lane * ext);
+    const float* b = bufs + (uint64_t)lane * ext;
+    float acc = b[0];
+    uint32_t c = 1;
+    for (; c < live && (c & 3); ++c) acc = __fadd_rn(acc, b[c]);
+    const uint32_t nv = (live - c) / 4;
+    uint32_t v = 0;
+    for (; v + 8 <= nv; v += 8) {
+      uint4 q[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) q[k] = lds_u4(base + (c + 4 * (v + k)) * 4);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        acc = __fadd_rn(acc, __uint_as_float(q[k].x));
+        acc = __fadd_rn(acc, __uint_as_float(q[k].y));
+        acc = __fadd_rn(acc, __uint_as_float(q[k].z));
+        acc = __fadd_rn(acc, __uint_as_float(q[k].w));
+      }
+    }
+    for (; v < nv; ++v) {
+      const uint4 q = lds_u4(base + (c + 4 * v) * 4);
+      acc = __fadd_rn(acc, __uint_as_float(q.x));
+      acc = __fadd_rn(acc, __uint_as_float(q.y));
+      acc = __fadd_rn(acc, __uint_as_float(q.z));
+      acc = __fadd_rn(acc, __uint_as_float(q.w));
+    }
+    for (c += 4 * nv; c < live; ++c) acc = __fadd_rn(acc, b[c]);
+    const float r = __fdiv_rn(1.0f, acc);
+    rcp[lane] = (poisoned[lane] || is_nan_bits(r)) ? __uint_as_float(kCanonicalNan) : r;
+  }
+}
+
+// Step 4: out = e * r (softmax.rs:306-312) in place over the row's live
+// columns, then one bulk store of the row (committed as a bulk group of the
+// calling lane 0).
+__device__ __forceinline__ void softmax_row_store(float* rowbuf, uint64_t row, uint32_t lane, float r, bool causal,
+                                                  uint64_t period, uint64_t row_offset, uint64_t extent,
+                                                  float* __restrict__ y) {
+  const uint32_t ext = (uint32_t)extent, row_bytes = ext * 4;
+  float4* b4 = reinterpret_cast<float4*>(rowbuf);
+  if (is_nan_bits(r)) {
+    const float nanv = __uint_as_float(kCanonicalNan);
+    for (uint32_t v = lane; v < ext / 4; v += 32) b4[v] = make_float4(nanv, nanv, nanv, nanv);
+  } else {
+    // e is finite and >= 0 and r finite: the product is never NaN; the
+    // masked tail already holds zeros (0 * r = +0)
+    const uint64_t row_live = causal ? umin64((row_offset + row) % period + 1, extent) : extent;
+    const uint32_t nv = (uint32_t)((row_live + 3) / 4);
+    for (uint32_t v = lane; v < nv; v += 32) {
+      const float4 q = b4[v];
+      b4[v] = make_float4(__fmul_rn(q.x, r), __fmul_rn(q.y, r), __fmul_rn(q.z, r), __fmul_rn(q.w, r));
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(y + row * extent),
+                 "r"(smem_u32(b4)), "r"(row_bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+}
+
 __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM)
     softmax_group_kernel(const float* __restrict__ x, uint64_t rows, uint64_t extent, uint64_t period,
                          uint64_t row_offset, float* __restrict__ y, uint32_t group, tiler_cuda_status* st,
@@ -698,129 +899,8 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
     }
 
     if (!chain_warp && warp < n) {
-      // ---- max and exponentials for row `warp` ---------------------------------
-      const uint64_t row = row0 + warp;
-      const uint32_t live = causal ? (uint32_t)umin64((row_offset + row) % period + 1, extent) : ext;
-      float* b = bufs + (uint64_t)warp * ext;
-      float4* b4 = reinterpret_cast<float4*>(b);
-      float m = __uint_as_float(0xff800000u);
-      const uint32_t live4 = live / 4;
-      if (mask) {
-        // the program's additive mask (an add-f32 of a broadcast mask tensor,
-        // standard.rs:211-221): t = x + mask[row mod mask_rows], one rounding,
-        // NaN canonicalized, written back in place before the maximum
-        const float4* m4 = reinterpret_cast<const float4*>(mask + ((row_offset + row) % mask_rows) * extent);
-        for (uint32_t v = lane; v < live4; v += 32) {
-          const float4 q = b4[v], a = __ldg(m4 + v);
-          const float4 t = make_float4(canon(__fadd_rn(q.x, a.x)), canon(__fadd_rn(q.y, a.y)),
-                                       canon(__fadd_rn(q.z, a.z)), canon(__fadd_rn(q.w, a.w)));
-          b4[v] = t;
-          m = max_nan(max_nan(m, t.x), max_nan(t.y, max_nan(t.z, t.w)));
-        }
-      } else {
-        for (uint32_t v = lane; v < live4; v += 32) {
-          const float4 q = b4[v];
-          m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
-        }
-      }
-      for (uint32_t c = live4 * 4 + lane; c < live; c += 32) m = max_nan(m, b[c]);
-      uint32_t bad = 0;  // a masked x that is NaN or +inf poisons the row
-      const uint32_t mask4 = (live + 3) / 4;  // first whole masked vector
-      auto poison = [](uint32_t xb) { return (uint32_t)(((xb & 0x7fffffffu) > 0x7f800000u) | (xb == 0x7f800000u)); };
-      for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) bad |= poison(__float_as_uint(b[c]));
-      for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) {
-        const uint4 q = reinterpret_cast<const uint4*>(b)[v];
-        bad |= poison(q.x) | poison(q.y) | poison(q.z) | poison(q.w);
-      }
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
-      bad = __any_sync(0xffffffffu, bad != 0);
-      // m is -inf only if every unmasked x is -inf: x - m is then NaN
-      auto exp_of = [&](float xv) {
-        const float sh = __fsub_rn(xv, m);
-        return sh > -104.0f ? exp_cr_fast(sh, table, st) : (is_nan_bits(sh) ? __uint_as_float(kCanonicalNan) : 0.0f);
-      };
-      uint32_t last_nz = 0;  // one past this lane's last nonzero e (mask tensor only)
-      // TRACK (a mask tensor): arguments at or below -104 give +0 without
-      // certification and the last nonzero e is tracked, so the fold can stop
-      // there; the in-kernel causal mask already stops at the diagonal
-      auto exp_pass = [&](auto track) {
-        constexpr bool TRACK = decltype(track)::value;
-        constexpr int EV = TILER_SMX_EXP_VECS;  // float4s per lane per step: 4 * EV independent exps
-        for (uint32_t v0 = lane; v0 < live4; v0 += 32 * EV) {
-          float xs[4 * EV];
-          uint32_t e[4 * EV], flagged = 0;
-#pragma unroll
-          for (int h = 0; h < EV; ++h) {
-            const uint32_t v = v0 + 32 * h;
-            const float4 q = v < live4 ? b4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
-            xs[4 * h] = q.x; xs[4 * h + 1] = q.y; xs[4 * h + 2] = q.z; xs[4 * h + 3] = q.w;
-          }
-          if (TRACK) {
-            // a step whose arguments are all at or below -104 (a masked stretch)
-            // is +0 throughout: skip the evaluation when the whole warp agrees
-            bool low = true;
-#pragma unroll
-            for (int i = 0; i < 4 * EV; ++i) {
-              const float sh = __fsub_rn(xs[i], m);
-              low = low && !(sh > -104.0f) && !is_nan_bits(sh);
-            }
-            if (__all_sync(__activemask(), low)) {
-#pragma unroll
-              for (int h = 0; h < EV; ++h) {
-                const uint32_t v = v0 + 32 * h;
-                if (v < live4) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-              }
-              continue;
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 4 * EV; ++i) {
-            const float sh = __fsub_rn(xs[i], m);
-            bool ok;
-            e[i] = exp_cr_bits(sh, table, &ok);
-            if (TRACK) {
-              // e^sh = +0 for sh <= -104 (silu.rs:224-235 guards): no certification needed
-              const bool zero = !(sh > -104.0f) && !is_nan_bits(sh);
-              if (zero) e[i] = 0u;
-              flagged |= ((ok && sh > -104.0f) || zero ? 0u : 1u) << i;
-            } else {
-              flagged |= ((ok && sh > -104.0f) ? 0u : 1u) << i;
-            }
-          }
-          if (__any_sync(__activemask(), flagged != 0)) {  // rare: certify or special-case the flagged ones
-#pragma unroll
-            for (int i = 0; i < 4 * EV; ++i)
-              if ((flagged >> i) & 1u) e[i] = __float_as_uint(softmax_exp_slow(__fsub_rn(xs[i], m), table, st));
-          }
-#pragma unroll
-          for (int h = 0; h < EV; ++h) {
-            const uint32_t v = v0 + 32 * h;
-            if (v < live4) {
-              b4[v] = make_float4(__uint_as_float(e[4 * h]), __uint_as_float(e[4 * h + 1]),
-                                  __uint_as_float(e[4 * h + 2]), __uint_as_float(e[4 * h + 3]));
-              if (TRACK) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                  if (e[4 * h + i] != 0u) last_nz = max(last_nz, v * 4 + i + 1);
-              }
-            }
-          }
-        }
-      };
-      if (mask) exp_pass(std::true_type{});
-      else exp_pass(std::false_type{});
-      for (uint32_t c = live4 * 4 + lane; c < live; c += 32) {
-        b[c] = exp_of(b[c]);
-        if (mask && __float_as_uint(b[c]) != 0u) last_nz = max(last_nz, c + 1);
-      }
-      for (uint32_t c = live + lane; c < mask4 * 4 && c < ext; c += 32) b[c] = 0.0f;
-      for (uint32_t v = mask4 + lane; v < ext / 4; v += 32) b4[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (mask) last_nz = __reduce_max_sync(0xffffffffu, last_nz);
-      if (lane == 0) {
-        poisoned[warp] = bad;
-        fold_end[warp] = mask ? max(last_nz, 1u) : live;  // at least e_0, the seed
-      }
+      softmax_row_exp(bufs + (uint64_t)warp * ext, row0 + warp, lane, extent, causal, period, row_offset, mask,
+                      mask_rows, table, st, &poisoned[warp], &fold_end[warp]);
     }
     if (!__syncthreads_and(ok)) {
       if (lane == 0 && !chain_warp) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -828,68 +908,13 @@ __global__ void __launch_bounds__(32 * (kSmxMaxGroup + 1), TILER_SMX_CTAS_PER_SM
     }
 
     if (chain_warp) {
-      // ---- chain warp: lane r folds row r's denominator ------------------------
-      if (lane < n) {
-        const uint32_t live = fold_end[lane];  // the unmasked columns up to the last nonzero e
-        const uint32_t base = smem_u32(bufs + (uint64_t)lane * ext);
-        const float* b = bufs + (uint64_t)lane * ext;
-        float acc = b[0];
-        uint32_t c = 1;
-        for (; c < live && (c & 3); ++c) acc = __fadd_rn(acc, b[c]);
-        const uint32_t nv = (live - c) / 4;
-        uint32_t v = 0;
-        for (; v + 8 <= nv; v += 8) {
-          uint4 q[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) q[k] = lds_u4(base + (c + 4 * (v + k)) * 4);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            acc = __fadd_rn(acc, __uint_as_float(q[k].x));
-            acc = __fadd_rn(acc, __uint_as_float(q[k].y));
-            acc = __fadd_rn(acc, __uint_as_float(q[k].z));
-            acc = __fadd_rn(acc, __uint_as_float(q[k].w));
-          }
-        }
-        for (; v < nv; ++v) {
-          const uint4 q = lds_u4(base + (c + 4 * v) * 4);
-          acc = __fadd_rn(acc, __uint_as_float(q.x));
-          acc = __fadd_rn(acc, __uint_as_float(q.y));
-          acc = __fadd_rn(acc, __uint_as_float(q.z));
-          acc = __fadd_rn(acc, __uint_as_float(q.w));
-        }
-        for (c += 4 * nv; c < live; ++c) acc = __fadd_rn(acc, b[c]);
-        const float r = __fdiv_rn(1.0f, acc);
-        rcp[lane] = (poisoned[lane] || is_nan_bits(r)) ? __uint_as_float(kCanonicalNan) : r;
-      }
+      softmax_chain_fold(lane, n, bufs, ext, fold_end, poisoned, rcp);
     }
     __syncthreads();
 
     if (!chain_warp && warp < n) {
-      // ---- out = e * r (softmax.rs:306-312), written in place, then one bulk store
-      const uint64_t row = row0 + warp;
-      const float r = rcp[warp];
-      float4* b4 = reinterpret_cast<float4*>(bufs + (uint64_t)warp * ext);
-      if (is_nan_bits(r)) {
-        const float nanv = __uint_as_float(kCanonicalNan);
-        for (uint32_t v = lane; v < ext / 4; v += 32) b4[v] = make_float4(nanv, nanv, nanv, nanv);
-      } else {
-        // e is finite and >= 0 and r finite: the product is never NaN; the
-        // masked tail already holds zeros (0 * r = +0)
-        const uint64_t row_live = causal ? umin64((row_offset + row) % period + 1, extent) : extent;
-        const uint32_t nv = (uint32_t)((row_live + 3) / 4);
-        for (uint32_t v = lane; v < nv; v += 32) {
-          const float4 q = b4[v];
-          b4[v] = make_float4(__fmul_rn(q.x, r), __fmul_rn(q.y, r), __fmul_rn(q.z, r), __fmul_rn(q.w, r));
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(y + row * extent),
-                     "r"(smem_u32(b4)), "r"(row_bytes)
-                     : "memory");
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      }
+      softmax_row_store(bufs + (uint64_t)warp * ext, row0 + warp, lane, rcp[warp], causal, period, row_offset, extent,
+                        y);
     }
     // no barrier here: a row warp reloads only its own buffer, after its store
   }
