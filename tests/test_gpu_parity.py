@@ -686,7 +686,12 @@ def test_gemm_bf16_full_config_sampled_rows(fam, oracle_lib):
     a = (torch.randn(m, k, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
     b = (torch.randn(n, k, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
     c = fam.gemm_bf16(a, b, epilogue="silu")
-    rows = [0, 1, 127, 128, 4095, 8191]
+    # one row from each CTA of every 256-row pair tile (rows 0-127 of a tile
+    # come from the first CTA's accumulator, 128-255 from the second's), plus
+    # the tile edges at both ends
+    rng = np.random.default_rng(17)
+    rows = sorted({0, 1, 127, 128, 255, 4095, 8191} |
+                  {t * 256 + h * 128 + int(rng.integers(0, 128)) for t in range(m // 256) for h in range(2)})
     an = a.view(torch.int16).cpu().numpy().view(np.uint16)
     bn = b.view(torch.int16).cpu().numpy().view(np.uint16)
     got = oracle_lib.bf16_to_f32(c.view(torch.int16).cpu().numpy().view(np.uint16)[rows])

@@ -432,6 +432,16 @@ __device__ __forceinline__ uint4 lds_u4(uint32_t saddr) {
   return v;
 }
 
+// Programmatic dependent launch (launch.cuh launches with it): a kernel may
+// start while the previous kernel on the stream finishes; it waits here,
+// before its first access to global memory, until that kernel has completed
+// and its writes are visible, then lets the next kernel start launching.
+// Without a programmatic dependency both are no-ops.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void sts_u4(uint32_t saddr, const uint4& v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(saddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");

@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -124,7 +125,26 @@ inline cudaError_t launch_kernel(const void* fn, const char* name, dim3 grid, di
       return cudaSuccess;
     }
   }
-  return cudaLaunchKernel(fn, grid, block, params, smem, stream);
+  // programmatic dependent launch: the kernel may begin while the previous
+  // kernel on the stream drains (every kernel launched here waits for it in
+  // grid_dependency_wait before touching global memory); TILER_PDL=0 in the
+  // environment (read once per process) launches plainly
+  static const bool pdl = [] {
+    const char* v = getenv("TILER_PDL");
+    return !(v && strcmp(v, "0") == 0);
+  }();
+  if (!pdl) return cudaLaunchKernel(fn, grid, block, params, smem, stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, params);
 }
 
 }  // namespace tc

@@ -195,6 +195,7 @@ __device__ __forceinline__ void grouped_fold(const float* __restrict__ x, uint64
   extern "C" __global__ void __launch_bounds__(1024)                                                       \
       NAME(const float* __restrict__ x, uint64_t count, tc::GroupedParams gp, float* __restrict__ partials, \
            unsigned int* __restrict__ tickets, float* __restrict__ out) {                                  \
+    tc::grid_dependency_wait();                                                                            \
     tc::grouped_fold<OP, K>(x, count, gp, partials, tickets, out);                                         \
   }
 TILER_GROUPED_KERNEL(tiler_grouped_sum_k1, 0, 1)

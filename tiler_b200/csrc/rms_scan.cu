@@ -289,12 +289,15 @@ __device__ __forceinline__ void rms_norm_scan(const uint8_t* __restrict__ x, con
   const uint8_t *__restrict__ x, const uint8_t *__restrict__ w, uint64_t rows, uint32_t extent, float eps,     \
       uint8_t *__restrict__ y, tiler_cuda_status *st, int8_t *__restrict__ codes, float *__restrict__ scales
 extern "C" __global__ void __launch_bounds__(tc::kRsThreads, 1) tiler_rms_norm_f32(TILER_RS_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_scan<false, false>(x, w, rows, extent, eps, y, st, codes, scales);
 }
 extern "C" __global__ void __launch_bounds__(tc::kRsThreads, 1) tiler_rms_norm_bf16(TILER_RS_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_scan<true, false>(x, w, rows, extent, eps, y, st, codes, scales);
 }
 extern "C" __global__ void __launch_bounds__(tc::kRsThreads, 1) tiler_rms_norm_quantize_i8(TILER_RS_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_scan<false, true>(x, w, rows, extent, eps, y, st, codes, scales);
 }
 #undef TILER_RS_PARAMS

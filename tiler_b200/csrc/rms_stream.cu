@@ -456,16 +456,19 @@ __device__ __forceinline__ void rms_norm_stream(const uint8_t* __restrict__ x, c
       uint8_t *__restrict__ y, tiler_cuda_status *st
 extern "C" __global__ void __launch_bounds__(tc::RmsStreamF32::kThreads, 1)
     tiler_rms_norm_stream_f32(TILER_RMS_STREAM_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_stream<tc::RmsElem<false>, tc::RmsStreamF32>(x, w, rows, extent, eps, y, st);
 }
 extern "C" __global__ void __launch_bounds__(tc::RmsStreamBF16::kThreads, 1)
     tiler_rms_norm_stream_bf16(TILER_RMS_STREAM_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_stream<tc::RmsElem<true>, tc::RmsStreamBF16>(x, w, rows, extent, eps, y, st);
 }
 extern "C" __global__ void __launch_bounds__(tc::RmsStreamF32::kThreads, 1)
     tiler_rms_norm_stream_quantize_i8(const uint8_t* __restrict__ x, const uint8_t* __restrict__ w, uint64_t rows,
                                       uint64_t extent, float eps, int8_t* __restrict__ codes,
                                       float* __restrict__ scales, tiler_cuda_status* st) {
+  tc::grid_dependency_wait();
   tc::rms_norm_stream<tc::RmsElem<false>, tc::RmsStreamF32, true>(x, w, rows, extent, eps, nullptr, st, codes,
                                                                  scales);
 }

@@ -477,13 +477,16 @@ __device__ __forceinline__ void rms_norm_wave(const uint8_t* __restrict__ x, con
       uint64_t extent, float eps, uint8_t *__restrict__ y, uint32_t wave_rows, tiler_cuda_status *st,          \
       int8_t *__restrict__ codes, float *__restrict__ scales
 extern "C" __global__ void __launch_bounds__(tc::kRmsThreads, 1) tiler_rms_norm_wave_f32(TILER_RMS_WAVE_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_wave<false, false>(x, w, w_row_stride, rows, extent, eps, y, wave_rows, st, codes, scales);
 }
 extern "C" __global__ void __launch_bounds__(tc::kRmsThreads, 1) tiler_rms_norm_wave_bf16(TILER_RMS_WAVE_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_wave<true, false>(x, w, w_row_stride, rows, extent, eps, y, wave_rows, st, codes, scales);
 }
 extern "C" __global__ void __launch_bounds__(tc::kRmsThreads, 1)
     tiler_rms_norm_wave_quantize_i8(TILER_RMS_WAVE_PARAMS) {
+  tc::grid_dependency_wait();
   tc::rms_norm_wave<false, true>(x, w, w_row_stride, rows, extent, eps, y, wave_rows, st, codes, scales);
 }
 #undef TILER_RMS_WAVE_PARAMS
