@@ -169,6 +169,15 @@ __device__ __forceinline__ float rms_fold_chunk(float acc, uint32_t p, uint32_t 
   return acc;
 }
 
+// A chunk shorter than the configured chunk (the last chunk of a row that is
+// not a multiple of it), out of line: the full chunks call the fold with
+// their length as a compile-time constant, which the compiler schedules
+// better (f32 RMS [8192,4096] 59.2 -> 57.6 us, bf16 50.3 -> 44.0 us).
+template <class E>
+__device__ __noinline__ float rms_fold_chunk_partial(float acc, uint32_t p, uint32_t nvec) {
+  return rms_fold_chunk<E>(acc, p, nvec);
+}
+
 // QUANT: the fused RMS norm -> per-row int8 quantize (f32 only): the
 // normalize warps keep y in registers, combine each row's max |y| across
 // the chunk owners (shared-memory atomics and one named barrier per group)
@@ -256,8 +265,12 @@ __device__ __forceinline__ void rms_norm_stream(const uint8_t* __restrict__ x, c
       const bool valid = lane_on && t >= 0 && t < G && r < group_rows(t);
       // the fold starts from +0 at chunk 0: +0 + a_0 is a_0 exactly (squares
       // are never -0), the reference's seed at the first square
-      if (valid) acc = rms_fold_chunk<E>(k == 0 ? 0.0f : prev_acc, lane_ring + (uint32_t)(slot * R * PITCH),
-                                         lane_bytes / 16);
+      if (valid) {
+        const float a0 = k == 0 ? 0.0f : prev_acc;
+        const uint32_t p = lane_ring + (uint32_t)(slot * R * PITCH);
+        acc = lane_bytes == (uint32_t)Cfg::CB ? rms_fold_chunk<E>(a0, p, Cfg::CB / 16)
+                                              : rms_fold_chunk_partial<E>(a0, p, lane_bytes / 16);
+      }
       // the group that finished its last chunk this step: its sums go to the
       // normalize warps, which form the scales off the chain's path
       const int tf = b - (nch - 1);
