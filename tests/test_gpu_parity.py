@@ -469,6 +469,30 @@ def test_silu_dense_sweep_and_ragged_tail_match_oracle(fam, oracle_lib):
     assert_bits_equal(got, want, "silu sweep")
 
 
+def test_silu_staged_division_matches_ieee_division_on_every_argument(fam):
+    """The staged SiLU map divides by Markstein's method (hardware reciprocal
+    estimate, one Newton step, one remainder correction) and the unaligned
+    form by the IEEE division; over every binary32 argument (2^32 bit
+    patterns, in chunks) the two give the same bits.  The unaligned form is
+    reached through a buffer offset by one element."""
+    chunk = 1 << 28
+    base = torch.arange(chunk, dtype=torch.int64, device="cuda")
+    xbuf = torch.empty(chunk + 1, dtype=torch.float32, device="cuda")
+    ya = torch.empty(chunk, dtype=torch.float32, device="cuda")
+    ybuf = torch.empty(chunk + 1, dtype=torch.float32, device="cuda")
+    for c in range(1 << 32 >> 28):
+        v = base + c * chunk
+        v = torch.where(v >= (1 << 31), v - (1 << 32), v).to(torch.int32).view(torch.float32)
+        xs = xbuf[1:]
+        xs.copy_(v)
+        fam.silu(v, out=ya, check=False)
+        fam.silu(xs, out=ybuf[1:], check=False)
+        diff = ya.view(torch.int32) != ybuf[1:].view(torch.int32)
+        n = int(diff.sum())
+        assert n == 0, f"chunk {c}: {n} mismatches, first arguments " + str(
+            [hex(int(u) & 0xffffffff) for u in v.view(torch.int32)[torch.nonzero(diff)[:4].flatten()]])
+
+
 def test_softmax_exp_band_sweep_matches_oracle(fam, oracle_lib):
     """Every exponent band the certified exp covers: rows of x with max 0, so
     exp(x) is evaluated on [-104, 0] densely."""

@@ -41,9 +41,10 @@ __device__ __noinline__ float silu_cr_outlined(float x, const double* table, til
   return silu_cr(x, table, st);
 }
 
-// SiLU of four values: silu_cr_fast's path for x in (-89, 104) with the
-// certified exp branch-free; the flagged values (out of range, NaN, or an exp
-// near a rounding midpoint) take silu_cr in one warp-uniform branch.
+// SiLU of four values: silu_cr_fast's path for x in (-87, 104) with the
+// certified exp and Markstein's division branch-free; the flagged values
+// (out of range, NaN, an exp near a rounding midpoint, or a quotient outside
+// the division's conditions) take silu_cr in one warp-uniform branch.
 struct SiluOp {
   const double* table;
   tiler_cuda_status* st;
@@ -53,10 +54,11 @@ struct SiluOp {
     uint32_t flagged = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      bool ok;
+      bool ok, ok_div;
       const float e = __uint_as_float(exp_cr_bits(-xs[i], table, &ok));
-      r[i] = __fdiv_rn(xs[i], __fadd_rn(1.0f, e));
-      flagged |= ((ok && xs[i] > -89.0f && xs[i] < 104.0f) ? 0u : 1u) << i;
+      r[i] = div_rn_markstein(xs[i], __fadd_rn(1.0f, e), &ok_div);
+      // x > -87 keeps exp(-x) below 2^126, as the division needs
+      flagged |= ((ok && ok_div && xs[i] > -87.0f && xs[i] < 104.0f) ? 0u : 1u) << i;
     }
     if (__any_sync(__activemask(), flagged != 0)) {
 #pragma unroll
