@@ -283,6 +283,9 @@ __device__ __forceinline__ float exp_cr_fast(float x, const double* table_hi, ti
 #define TILER_EXP_LEAN 1
 #endif
 constexpr double kLn2By256 = 0x1.62e42fefa39efp-9;  // RN(ln2 / 256)
+// kRangeChecked: the caller keeps x inside (-87, 88), where e^x is a normal
+// binary32 value, so only the midpoint window decides ok.
+template <bool kRangeChecked = false>
 __device__ __forceinline__ uint32_t exp_cr_bits(float x, const double* table_hi, bool* ok) {
   const double xd = (double)x;
   const double t = __fma_rn(xd, kInvLn2x256, kRoundShift);
@@ -305,8 +308,8 @@ __device__ __forceinline__ uint32_t exp_cr_bits(float x, const double* table_hi,
   const double y0 = __fma_rn(tj, p, tj);
   const uint32_t hi = (uint32_t)__double2hiint(y0) + ((uint32_t)(n >> 8) << 20);
   const uint32_t lo = (uint32_t)__double2loint(y0);
-  *ok = (hi - 0x38100000u) < (0x47f00000u - 0x38100000u) &&
-        ((lo & 0x1fffffffu) - (0x10000000u - kWindow)) > 2 * kWindow;
+  const bool window_ok = ((lo & 0x1fffffffu) - (0x10000000u - kWindow)) > 2 * kWindow;
+  *ok = kRangeChecked ? window_ok : (hi - 0x38100000u) < (0x47f00000u - 0x38100000u) && window_ok;
   // binary32 bits: exponent rebased, 23 mantissa bits from hi:lo, rounded by bit 28
   return __funnelshift_l(lo, hi - 0x38000000u, 3) + ((lo >> 28) & 1u);
 }

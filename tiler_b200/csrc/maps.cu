@@ -41,29 +41,28 @@ __device__ __noinline__ float silu_cr_outlined(float x, const double* table, til
   return silu_cr(x, table, st);
 }
 
-// SiLU of four values: silu_cr_fast's path for x in (-87, 104) with the
-// certified exp and Markstein's division branch-free; the flagged values
-// (out of range, NaN, an exp near a rounding midpoint, or a quotient outside
-// the division's conditions) take silu_cr in one warp-uniform branch.
+// SiLU of four values: for x in (-87, 87), where exp(-x) is a normal
+// binary32 value below 2^126, the certified exp and Markstein's division run
+// branch-free; a lane holding any other value (out of range, NaN, an exp near
+// a rounding midpoint, a quotient outside the division's conditions) redoes
+// its four values with silu_cr, the exact path, in one warp-uniform branch.
 struct SiluOp {
   const double* table;
   tiler_cuda_status* st;
   __device__ __forceinline__ float4 operator()(float4 q) const {
     const float xs[4] = {q.x, q.y, q.z, q.w};
     float r[4];
-    uint32_t flagged = 0;
+    bool all_ok = true;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       bool ok, ok_div;
-      const float e = __uint_as_float(exp_cr_bits(-xs[i], table, &ok));
+      const float e = __uint_as_float(exp_cr_bits<true>(-xs[i], table, &ok));
       r[i] = div_rn_markstein(xs[i], __fadd_rn(1.0f, e), &ok_div);
-      // x > -87 keeps exp(-x) below 2^126, as the division needs
-      flagged |= ((ok && ok_div && xs[i] > -87.0f && xs[i] < 104.0f) ? 0u : 1u) << i;
+      all_ok = all_ok && ok && ok_div && fabsf(xs[i]) < 87.0f;
     }
-    if (__any_sync(__activemask(), flagged != 0)) {
+    if (__any_sync(__activemask(), !all_ok) && !all_ok) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if ((flagged >> i) & 1u) r[i] = silu_cr_outlined(xs[i], table, st);
+      for (int i = 0; i < 4; ++i) r[i] = silu_cr_outlined(xs[i], table, st);
     }
     return make_float4(r[0], r[1], r[2], r[3]);
   }
