@@ -278,6 +278,9 @@ def family_suite(fam, torch, world, steps_small, warmup):
     """Per-family device throughput at the BASELINE configs (each config's own
     algorithmic bytes / FLOPs; rotating buffers so inputs exceed L2)."""
     hbm, tflops, _ = measured_peaks()
+    # the strong-scaled lines first, at the clocks the headline ran at (after
+    # the power-heavy contraction they measured up to 30 % slower)
+    strong = strong_scaled_suite(fam, torch, world, steps_small, warmup)
     out = {}
     gen = torch.Generator("cuda").manual_seed(7)
     dev = "cuda"
@@ -453,7 +456,7 @@ def family_suite(fam, torch, world, steps_small, warmup):
                        ("gemm_bf16_silu_8192x4096x14336", "gemm_bf16_silu_pair_2048x14336x4096.txt")):
         if name in out and os.path.exists(os.path.join(ROOT, "profiles", prof)):
             out[name]["profile"] = "profiles/" + prof
-    out.update(strong_scaled_suite(fam, torch, world, steps_small, warmup))
+    out.update(strong)
     return out
 
 

@@ -132,8 +132,8 @@ const Entry kEntries[] = {
     {"tiler_cuda.sum_f32.cooperative", (const void*)cooperative_sum_kernel, 1024, 0},
     {"tiler_cuda.rms_norm_f32", (const void*)tiler_rms_norm_stream_f32, RmsStreamF32::kThreads,
      rms_stream_smem_bytes<RmsStreamF32>(), "tiler_rms_norm_stream_f32"},
-    {"tiler_cuda.rms_norm_bf16", (const void*)tiler_rms_norm_wave_bf16, kRmsThreads, kRmsSmemBytes,
-     "tiler_rms_norm_wave_bf16"},
+    {"tiler_cuda.rms_norm_bf16", (const void*)tiler_rms_norm_stream_bf16, RmsStreamBF16::kThreads,
+     rms_stream_smem_bytes<RmsStreamBF16>(), "tiler_rms_norm_stream_bf16"},
     {"tiler_cuda.softmax_f32", (const void*)softmax_group_kernel, 32 * 7, 2048 + 256 + 6 * 8192},
     {"tiler_cuda.quantize_i8_rows", (const void*)quantize_i8_rows_kernel, kQThreads, 0},
     {"tiler_cuda.rms_norm_quantize_i8", (const void*)tiler_rms_norm_wave_quantize_i8, kRmsThreads, kRmsSmemBytes,

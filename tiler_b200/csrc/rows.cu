@@ -530,8 +530,8 @@ __global__ void rms_norm_generic_kernel(const void* __restrict__ xv, const void*
 // kernel where it applies: "scan" the warp-per-row kernel (rms_scan.cu),
 // "stream" the chunk-streamed kernel (rms_stream.cu), "wave" the wave kernel.
 // All are exact.  Unset, each family takes the form measured fastest on the
-// BASELINE shapes: the streamed kernel for f32 RMS (it reads x once), the
-// wave kernel for bf16 RMS and for the fused int8 quantize.
+// BASELINE shapes: the streamed kernel for f32 and bf16 RMS (it reads x
+// once), the wave kernel for the fused int8 quantize.
 enum RmsForm { kRmsFormAuto = 0, kRmsFormWave = 1, kRmsFormScan = 2, kRmsFormStream = 3 };
 static int rms_form_selected() {
   static const int form = [] {
@@ -588,7 +588,7 @@ int launch_rms_norm(int bf16, const void* x, const void* w, int64_t w_row_stride
       rms_scan_launch(bf16, 0, x, w, w_row_stride, rows, extent, eps, y, nullptr, nullptr, st, sm_count, stream))
     return 0;
   const int form = rms_form_selected();
-  if ((form == kRmsFormStream || (form == kRmsFormAuto && !bf16)) &&
+  if ((form == kRmsFormStream || form == kRmsFormAuto) &&
       rms_stream_launch(bf16, x, w, w_row_stride, rows, extent, eps, y, st, sm_count, stream))
     return 0;
   // One CTA per SM; each takes rows/grid consecutive rows in waves.
