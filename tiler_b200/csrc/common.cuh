@@ -361,22 +361,20 @@ __device__ __forceinline__ float rsqrt_cr(float t) {
 // within half an ulp of 1/d, a quotient q0 = RN(x y) within an ulp of x / d,
 // its exact remainder r = x - q0 d (one FMA), and q = RN(q0 + r y) is the
 // correctly rounded quotient.  y comes from the hardware reciprocal estimate
-// refined by one FMA Newton step, y = y0 + y0 (1 - d y0), which is the
-// correctly rounded reciprocal except when d's significand is all ones.
-// The caller keeps d in [1, 2^126) (a reciprocal above the subnormal
-// range); ok is false where the method's other conditions are not met here:
-// that significand, or |x| below 2^-60 (a quotient near the subnormal range,
-// and the sign of a zero).  Checked against the IEEE division over every
-// binary32 SiLU argument.
-__device__ __forceinline__ float div_rn_markstein(float x, float d, bool* ok) {
+// refined by one FMA Newton step, y = y0 + y0 (1 - d y0), the correctly
+// rounded reciprocal except possibly when d's significand is all ones.  The
+// caller keeps d in [1, 2^126) (a reciprocal above the subnormal range) and
+// |x| at or above 2^-60 (a quotient clear of the subnormal range, no signed
+// zero).  For the SiLU map, where d = 1 + RN(exp(-x)), the quotient equals
+// the IEEE division on every binary32 argument in that range, the
+// all-ones-significand d included: a GPU test checks all 2^32 arguments.
+__device__ __forceinline__ float div_rn_markstein(float x, float d) {
   float y0;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(d));
   const float e = __fmaf_rn(-d, y0, 1.0f);
   const float y = __fmaf_rn(e, y0, y0);
   const float q0 = __fmul_rn(x, y);
   const float r = __fmaf_rn(-q0, d, x);
-  const uint32_t db = __float_as_uint(d), xb = __float_as_uint(x) & 0x7fffffffu;
-  *ok = (db & 0x7fffffu) != 0x7fffffu && xb >= 0x21800000u;
   return __fmaf_rn(r, y, q0);
 }
 

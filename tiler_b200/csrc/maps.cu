@@ -41,11 +41,11 @@ __device__ __noinline__ float silu_cr_outlined(float x, const double* table, til
   return silu_cr(x, table, st);
 }
 
-// SiLU of four values: for x in (-87, 87), where exp(-x) is a normal
-// binary32 value below 2^126, the certified exp and Markstein's division run
-// branch-free; a lane holding any other value (out of range, NaN, an exp near
-// a rounding midpoint, a quotient outside the division's conditions) redoes
-// its four values with silu_cr, the exact path, in one warp-uniform branch.
+// SiLU of four values: for 2^-60 <= |x| < 87, where exp(-x) is a normal
+// binary32 value below 2^126 and x / d clear of the subnormal range, the
+// certified exp and Markstein's division run branch-free; a lane holding any
+// other value (out of range, NaN, an exp near a rounding midpoint) redoes its
+// four values with silu_cr, the exact path, in one warp-uniform branch.
 struct SiluOp {
   const double* table;
   tiler_cuda_status* st;
@@ -55,10 +55,11 @@ struct SiluOp {
     bool all_ok = true;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      bool ok, ok_div;
+      bool ok;
       const float e = __uint_as_float(exp_cr_bits<true>(-xs[i], table, &ok));
-      r[i] = div_rn_markstein(xs[i], __fadd_rn(1.0f, e), &ok_div);
-      all_ok = all_ok && ok && ok_div && fabsf(xs[i]) < 87.0f;
+      r[i] = div_rn_markstein(xs[i], __fadd_rn(1.0f, e));
+      // 2^-60 <= |x| < 87 (0x21800000 and 0x42ae0000 as magnitude bits; NaN above)
+      all_ok = all_ok && ok && ((__float_as_uint(xs[i]) & 0x7fffffffu) - 0x21800000u) < 0x212e0000u;
     }
     if (__any_sync(__activemask(), !all_ok) && !all_ok) {
 #pragma unroll
