@@ -451,6 +451,7 @@ def family_suite(fam, torch, world, steps_small, warmup):
                        ("dequantize_i8_16384x4096", "dequantize_sum_gather_launch_metrics.txt"),
                        ("gather_bf16_8192_of_128256x4096", "dequantize_sum_gather_launch_metrics.txt"),
                        ("silu_f32_8192x4096", "silu_f32_8192x4096.txt"),
+                       ("rms_norm_bf16_8192x4096", "rms_norm_bf16_8192x4096.txt"),
                        ("softmax_f32_65536x2048_causal", "softmax_f32_65536x2048_causal.txt"),
                        ("quantize_i8_16384x4096", "quantize_i8_16384x4096.txt"),
                        ("gemm_bf16_silu_8192x4096x14336", "gemm_bf16_silu_pair_2048x14336x4096.txt")):
