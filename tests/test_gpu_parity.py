@@ -223,8 +223,11 @@ def test_rms_norm_f32_matches_oracle(fam, oracle_lib, rows, extent, full_w):
     assert_bits_equal(got, want, f"rms f32 {rows}x{extent}")
 
 
-@pytest.mark.parametrize("rows,extent", [(8192, 4096), (77, 4096), (9, 100)])
+@pytest.mark.parametrize("rows,extent", [(8192, 4096), (77, 4096), (9, 100), (300, 4088), (50, 1000), (149, 4096)])
 def test_rms_norm_bf16_matches_oracle(fam, oracle_lib, rows, extent):
+    """The streamed bf16 kernel with full 1 KB chunks (4096), a short last
+    chunk (4088), only short chunks (1000) and about one row per CTA (149
+    rows); 100 elements (200-byte rows) take the unaligned kernel."""
     x = oracle_lib.f32_to_bf16(seeded_normal(rows + extent, rows * extent).reshape(rows, extent))
     w = oracle_lib.f32_to_bf16(seeded_uniform(4, extent, 0.5, 1.5))
     xt = cuda(x.view(np.int16)).view(torch.bfloat16)
