@@ -93,8 +93,11 @@ struct ScaleBiasOp {
 // the map's register footprint.  The last n % 4 elements are done by block 0
 // with plain accesses.
 constexpr int kMapThreads = 256;
-constexpr uint32_t kMapTile = 2048;  // floats (8 KB)
-constexpr uint32_t kMapStages = 4;
+// 16 KB tiles in a ring of 3: per thread four float4 per tile between the
+// tile's barriers (8 KB tiles in a ring of 4 measured SiLU 59.8 us and
+// scale-bias 46.1 us at [8192,4096], against 57.0 and 45.5 us)
+constexpr uint32_t kMapTile = 4096;  // floats (16 KB)
+constexpr uint32_t kMapStages = 3;
 constexpr int kMapCtasPerSm = 6;
 constexpr size_t kMapSmem = (size_t)kMapStages * kMapTile * 4 + kMapStages * 8;
 
