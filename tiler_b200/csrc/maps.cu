@@ -132,7 +132,15 @@ __device__ __forceinline__ void staged_map(const float* __restrict__ x, uint64_t
     if (abort_flag) break;
     const uint32_t nf = tile_floats(t);
     float4* v = reinterpret_cast<float4*>(buf + b * kMapTile);
-    for (uint32_t i = threadIdx.x; i < nf / 4; i += kMapThreads) v[i] = op(v[i]);
+    if (nf == kMapTile) {
+      // a full tile: a fixed number of vectors per thread, unrolled (SiLU
+      // 56.5 -> 55.5 us at [8192,4096])
+#pragma unroll
+      for (uint32_t j = 0; j < kMapTile / 4 / kMapThreads; ++j)
+        v[threadIdx.x + j * kMapThreads] = op(v[threadIdx.x + j * kMapThreads]);
+    } else {
+      for (uint32_t i = threadIdx.x; i < nf / 4; i += kMapThreads) v[i] = op(v[i]);
+    }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0) {
