@@ -38,13 +38,17 @@
 
 namespace tc {
 
-template <int P_, int R_, int CB_, int C_>
+template <int P_, int R_, int CB_, int C_, int PAD_ = 128>
 struct RmsStreamCfg {
   static constexpr int P = P_;    // chunks per row (at most)
   static constexpr int R = R_;    // rows per group
   static constexpr int CB = CB_;  // chunk bytes (at most)
   static constexpr int C = C_;    // extra slot lifetime (steps of producer lead)
-  static constexpr int kPitch = (CB + 127) / 128 * 128 + 128;
+  // buffer pitch: a 128-byte pad lets each (chunk, row) ring start 16 * (lane
+  // mod 8) bytes into it (conflict-free chain reads); a smaller pad spreads
+  // the buffers over the banks by the pitch alone
+  static constexpr bool kStagger = PAD_ >= 128;
+  static constexpr int kPitch = (CB + 127) / 128 * 128 + PAD_;
   static constexpr int kBuffers = (P * (P + 1) / 2 + C * P) * R;
   // mbarrier rings (batches, groups): the producer issues the first P + C
   // batches before it waits for anything, so the batch ring must hold them all
@@ -58,11 +62,13 @@ struct RmsStreamCfg {
 
 // f32 rows of up to 16 KB: 8 chunks of 2 KB, groups of 2 rows (16 chain lanes).
 using RmsStreamF32 = RmsStreamCfg<8, 2, 2048, 2>;
-// bf16 rows of up to 8 KB: 8 chunks of 1 KB, groups of 3 rows (24 chain lanes;
+// bf16 rows of up to 8 KB: 8 chunks of 1 KB, groups of 4 rows (32 chain lanes;
 // a bf16 row moves half the bytes of an f32 row for the same fold length),
-// slots living one step longer (C = 3: the producer runs a step further ahead,
-// 42.7 us against 44.2 us at C = 2 for [8192,4096]; f32 has no room for it).
-using RmsStreamBF16 = RmsStreamCfg<8, 3, 1024, 3>;
+// buffers 1072 bytes apart with no per-lane stagger so four rows fit (the
+// chain does 8 adds per 16-byte load, so a 2-way bank conflict costs little):
+// 40.6 us for [8192,4096] against 42.7 us with 3 rows and C = 3 and 44.2 us
+// with 3 rows and C = 2.
+using RmsStreamBF16 = RmsStreamCfg<8, 4, 1024, 2, 48>;
 
 template <class Cfg>
 struct RmsStreamSmem {
@@ -77,7 +83,10 @@ struct RmsStreamSmem {
   alignas(128) uint8_t buf[Cfg::kBuffers * Cfg::kPitch];
 };
 template <class Cfg>
-constexpr size_t rms_stream_smem_bytes() { return sizeof(RmsStreamSmem<Cfg>); }
+constexpr size_t rms_stream_smem_bytes() {
+  static_assert(sizeof(RmsStreamSmem<Cfg>) <= 227 * 1024, "one CTA's shared memory on sm_100a");
+  return sizeof(RmsStreamSmem<Cfg>);
+}
 
 // Warp roles: warp 0 folds, alone on its scheduler (a warp's scheduler is its
 // index mod 4, and warps 4 and 8 do nothing); warp 1 loads; warps 2, 3, 5, 6,
@@ -208,7 +217,7 @@ __device__ __forceinline__ void rms_norm_stream(const uint8_t* __restrict__ x, c
   // buffer of row r of chunk k sits 16 * ((k R + r) mod 8) bytes into its pitch
   auto ring_base = [&](int k, int r) -> uint32_t {
     const int base = k * (nch + C) - k * (k - 1) / 2;  // sum_{j<k} L_j
-    return smem_u32(S.buf) + (uint32_t)((base * R + r) * PITCH + 16 * ((k * R + r) & 7));
+    return smem_u32(S.buf) + (uint32_t)((base * R + r) * PITCH + (Cfg::kStagger ? 16 * ((k * R + r) & 7) : 0));
   };
 
   if (threadIdx.x == 0) {
